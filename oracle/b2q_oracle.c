@@ -1,0 +1,655 @@
+/*
+ * b2q_oracle.c — CPU restatement of the SigLIP2 Q8_0 x q8_1 hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY (see b2q_oracle.h): the checker for the CUDA path
+ * and the timed CPU baseline ("port").  Built with -ffp-contract=off so that
+ * every rounding step below is exactly the one written.
+ */
+#include "b2q_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* threading                                                                 */
+/* ------------------------------------------------------------------------ */
+int orc_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void) n;
+#endif
+}
+
+/* ------------------------------------------------------------------------ */
+/* fp16 <-> fp32 (IEEE binary16, round-to-nearest-even)                      */
+/* ggml block_q8_0::d is an fp16 (ggml-common.h block_q8_0; gguf quants.py:389) */
+/* ------------------------------------------------------------------------ */
+float orc_fp16_to_fp32(uint16_t h) {
+    _Float16 v;
+    memcpy(&v, &h, 2);
+    return (float) v;
+}
+
+uint16_t orc_fp32_to_fp16(float f) {
+    _Float16 v = (_Float16) f;
+    uint16_t h;
+    memcpy(&h, &v, 2);
+    return h;
+}
+
+/* ------------------------------------------------------------------------ */
+/* exp / tanh / GELU                                                         */
+/*                                                                           */
+/* The reference's GELU (src/cuda/siglip2_megakernel.cu:276-280) calls the   */
+/* platform tanhf.  CPU and GPU tanhf differ in the last bits, so this       */
+/* library uses its own tanh on both sides (same operations in the same      */
+/* order, every step an IEEE-exact +,*,fma,/): a Cody-Waite range-reduced    */
+/* exp (ln2 split into a 16-bit head and a tail) with the degree-8 Taylor    */
+/* polynomial of e^r on |r| <= ln2/2, and for |x| < 0.5625 the Maclaurin     */
+/* series of tanh to x^19.  Error vs. a correctly rounded tanh is tested to  */
+/* stay within 2 ulp (tests/test_oracle.py).                                 */
+/* ------------------------------------------------------------------------ */
+#define ORC_LOG2E   1.44269504088896340736f
+#define ORC_LN2_HI  0.693145751953125f          /* 0x3F317200 */
+#define ORC_LN2_LO  1.42860682030941723212e-6f  /* ln2 - LN2_HI */
+
+float orc_expf(float x) {
+    /* valid for |x| <= 80 (callers stay far inside) */
+    float n = rintf(x * ORC_LOG2E);
+    float r = fmaf(-n, ORC_LN2_HI, x);
+    r = fmaf(-n, ORC_LN2_LO, r);
+    float p = 2.48015873015873015873e-5f;            /* 1/8! */
+    p = fmaf(p, r, 1.98412698412698412698e-4f);      /* 1/7! */
+    p = fmaf(p, r, 1.38888888888888888889e-3f);      /* 1/6! */
+    p = fmaf(p, r, 8.33333333333333333333e-3f);      /* 1/5! */
+    p = fmaf(p, r, 4.16666666666666666667e-2f);      /* 1/4! */
+    p = fmaf(p, r, 1.66666666666666666667e-1f);      /* 1/3! */
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    /* scale by 2^n through the exponent field */
+    int32_t ni = (int32_t) n;
+    union { float f; int32_t i; } s;
+    s.i = (ni + 127) << 23;
+    return p * s.f;
+}
+
+float orc_tanhf(float x) {
+    float ax = fabsf(x);
+    float y;
+    if (ax < 0.5625f) {
+        /* Maclaurin coefficients 2^2n (2^2n - 1) B_2n / (2n)! of x^(2n-1),
+         * n = 2..10, rounded to fp32 */
+        const float c1 = -3.33333343267440795898e-01f;   /* -1/3                      */
+        const float c2 =  1.33333340287208557129e-01f;   /*  2/15                     */
+        const float c3 = -5.39682544767856597900e-02f;   /* -17/315                   */
+        const float c4 =  2.18694880604743957520e-02f;   /*  62/2835                  */
+        const float c5 = -8.86323582381010055542e-03f;   /* -1382/155925              */
+        const float c6 =  3.59212793409824371338e-03f;   /*  21844/6081075            */
+        const float c7 = -1.45583436824381351471e-03f;   /* -929569/638512875         */
+        const float c8 =  5.90027426369488239288e-04f;   /*  6404582/10854718875      */
+        const float c9 = -2.39129120018333196640e-04f;   /* -443861162/1856156927625  */
+        float x2 = x * x;
+        float q = c9;
+        q = fmaf(q, x2, c8);
+        q = fmaf(q, x2, c7);
+        q = fmaf(q, x2, c6);
+        q = fmaf(q, x2, c5);
+        q = fmaf(q, x2, c4);
+        q = fmaf(q, x2, c3);
+        q = fmaf(q, x2, c2);
+        q = fmaf(q, x2, c1);
+        float x3 = x2 * x;
+        return fmaf(q, x3, x);
+    } else if (ax < 9.0f) {
+        float e = orc_expf(2.0f * ax);
+        y = 1.0f - 2.0f / (e + 1.0f);
+    } else {
+        y = 1.0f;
+    }
+    return copysignf(y, x);
+}
+
+float orc_gelu(float x) {
+    /* siglip2_megakernel.cu:276-280, evaluated left to right without
+     * contraction: 0.5*x*(1+tanh(c*x*(1+a*x*x))) */
+    const float GELU_COEF_A    = 0.044715f;
+    const float SQRT_2_OVER_PI = 0.79788456080286535587989211986876f;
+    float x2    = x * x;
+    float inner = 1.0f + GELU_COEF_A * x2;
+    float arg   = (SQRT_2_OVER_PI * x) * inner;
+    float t     = orc_tanhf(arg);
+    return (0.5f * x) * (1.0f + t);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Q8_0 weight codec — gguf-py quants.py:381-401 (bit-exact with            */
+/* ggml-quants.c quantize_row_q8_0_ref): d = max|x|/127 in fp32,             */
+/* id = d ? 1/d : 0, q = roundf(x*id) (half away from zero), d stored fp16.  */
+/* ------------------------------------------------------------------------ */
+void orc_quantize_q8_0(const float *x, int64_t N, int64_t K, int64_t Kp, uint8_t *out) {
+    const int64_t Kb = Kp / 32;
+    #pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < N; ++n) {
+        for (int64_t kb = 0; kb < Kb; ++kb) {
+            float v[32];
+            for (int j = 0; j < 32; ++j) {
+                int64_t k = kb * 32 + j;
+                v[j] = (k < K) ? x[n * K + k] : 0.0f;
+            }
+            float amax = 0.0f;
+            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+            float d  = amax / 127.0f;
+            float id = (d != 0.0f) ? 1.0f / d : 0.0f;
+            uint8_t *blk = out + (n * Kb + kb) * 34;
+            uint16_t dh = orc_fp32_to_fp16(d);
+            memcpy(blk, &dh, 2);
+            for (int j = 0; j < 32; ++j) {
+                float q = roundf(v[j] * id);
+                blk[2 + j] = (uint8_t) (int8_t) q;
+            }
+        }
+    }
+}
+
+void orc_dequantize_q8_0(const uint8_t *w, int64_t N, int64_t Kp, float *out) {
+    const int64_t Kb = Kp / 32;
+    #pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < N; ++n) {
+        for (int64_t kb = 0; kb < Kb; ++kb) {
+            const uint8_t *blk = w + (n * Kb + kb) * 34;
+            uint16_t dh;
+            memcpy(&dh, blk, 2);
+            float d = orc_fp16_to_fp32(dh);
+            for (int j = 0; j < 32; ++j)
+                out[n * Kp + kb * 32 + j] = (float) (int8_t) blk[2 + j] * d;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* q8_1 activation quantize — src/cuda/siglip2_custom_mmq.cu:51-82:          */
+/* a = max|x| over the 32-block, d = a/127, q = rint(x * 127/a) (round half  */
+/* to even, __float2int_rn) clamped to [-128,127]; a == 0 gives q = 0.       */
+/* Columns K..Kp-1 are zero (pad_x_to_w, siglip2_vision.cpp:99-107).         */
+/* ------------------------------------------------------------------------ */
+static inline void q8_1_block(const float *v, int8_t *q, float *d) {
+    float a = 0.0f;
+    for (int j = 0; j < 32; ++j) a = fmaxf(a, fabsf(v[j]));
+    float inv = (a == 0.0f) ? 0.0f : 127.0f / a;
+    *d = a / 127.0f;
+    for (int j = 0; j < 32; ++j) {
+        float r = rintf(v[j] * inv);
+        if (r > 127.0f) r = 127.0f;
+        if (r < -128.0f) r = -128.0f;
+        q[j] = (int8_t) r;
+    }
+}
+
+void orc_quantize_q8_1(const float *x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
+                       int8_t *qs, float *d) {
+    const int64_t Kb = Kp / 32;
+    #pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t kb = 0; kb < Kb; ++kb) {
+            float v[32];
+            for (int j = 0; j < 32; ++j) {
+                int64_t k = kb * 32 + j;
+                v[j] = (k < K) ? x[m * ldx + k] : 0.0f;
+            }
+            q8_1_block(v, qs + m * Kp + kb * 32, d + m * Kb + kb);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Block GEMM — ggml_mul_mat(W Q8_0, X) semantics as restated by            */
+/* src/cuda/siglip2_custom_mmq.cu:229-266: per K-block int32 dot, then       */
+/* Cf += (float)Cint * dw * dx, evaluated as fma((float)S*dw, dx, acc).      */
+/* ------------------------------------------------------------------------ */
+__attribute__((target_clones("arch=x86-64-v4", "arch=x86-64-v3", "default")))
+static int32_t dot32_i8(const int8_t *a, const int8_t *b) {
+    int32_t s = 0;
+    for (int j = 0; j < 32; ++j) s += (int32_t) a[j] * (int32_t) b[j];
+    return s;
+}
+
+void orc_gemm_q8(const uint8_t *w, int64_t N, int64_t Kp,
+                 const int8_t *qs, const float *dx, int64_t M,
+                 float *y, int32_t *block_sums) {
+    const int64_t Kb = Kp / 32;
+    /* unpack weights once: int8 plane + fp32 scales (exact fp16 widening) */
+    int8_t *wq = (int8_t *) malloc((size_t) N * (size_t) Kp);
+    float  *wd = (float *) malloc((size_t) N * (size_t) Kb * sizeof(float));
+    #pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < N; ++n) {
+        for (int64_t kb = 0; kb < Kb; ++kb) {
+            const uint8_t *blk = w + (n * Kb + kb) * 34;
+            uint16_t dh;
+            memcpy(&dh, blk, 2);
+            wd[n * Kb + kb] = orc_fp16_to_fp32(dh);
+            memcpy(wq + n * Kp + kb * 32, blk + 2, 32);
+        }
+    }
+    #pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t m = 0; m < M; ++m) {
+        const int8_t *xr = qs + m * Kp;
+        const float  *xd = dx + m * Kb;
+        for (int64_t n = 0; n < N; ++n) {
+            const int8_t *wr = wq + n * Kp;
+            const float  *wdr = wd + n * Kb;
+            float acc = 0.0f;
+            for (int64_t kb = 0; kb < Kb; ++kb) {
+                int32_t S = dot32_i8(xr + kb * 32, wr + kb * 32);
+                if (block_sums) block_sums[(m * N + n) * Kb + kb] = S;
+                float t = (float) S * wdr[kb];
+                acc = fmaf(t, xd[kb], acc);
+            }
+            y[m * N + n] = acc;
+        }
+    }
+    free(wq);
+    free(wd);
+}
+
+/* ------------------------------------------------------------------------ */
+/* LayerNorm + affine — src/cuda/siglip2_megakernel.cu:81-121.               */
+/* One-pass sums.  Summation order (shared with the CUDA row kernel): lane   */
+/* l in 0..31 accumulates elements (c*32 + l)*4 + j for c ascending, j in    */
+/* 0..3, s += v and ss = fma(v, v, ss); the 32 lane partials are combined by */
+/* an xor butterfly with offsets 16, 8, 4, 2, 1.  H must be a multiple of    */
+/* 128.  mean = s/H, var = ss/H - mean*mean, inv = 1/sqrt(var + eps).        */
+/* y = ((x - mean) * inv) * w + b with separately rounded steps.             */
+/* ------------------------------------------------------------------------ */
+static void row_moments(const float *x, int64_t H, float *mean_out, float *inv_unused, float *s_out, float *ss_out) {
+    (void) inv_unused;
+    float ps[32], pss[32];
+    const int64_t chunks = H / 128;
+    for (int l = 0; l < 32; ++l) {
+        float s = 0.0f, ss = 0.0f;
+        for (int64_t c = 0; c < chunks; ++c) {
+            for (int j = 0; j < 4; ++j) {
+                float v = x[(c * 32 + l) * 4 + j];
+                s  = s + v;
+                ss = fmaf(v, v, ss);
+            }
+        }
+        ps[l] = s;
+        pss[l] = ss;
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+        float ns[32], nss[32];
+        for (int l = 0; l < 32; ++l) {
+            ns[l]  = ps[l] + ps[l ^ off];
+            nss[l] = pss[l] + pss[l ^ off];
+        }
+        memcpy(ps, ns, sizeof ps);
+        memcpy(pss, nss, sizeof pss);
+    }
+    *s_out = ps[0];
+    *ss_out = pss[0];
+    *mean_out = ps[0] / (float) H;
+}
+
+void orc_layernorm(const float *x, const float *w, const float *b, float eps,
+                   int64_t M, int64_t H, float *y) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        const float *xr = x + m * H;
+        float mean, s, ss;
+        row_moments(xr, H, &mean, NULL, &s, &ss);
+        float msq = ss / (float) H;
+        float var = msq - mean * mean;
+        float inv = 1.0f / sqrtf(var + eps);
+        for (int64_t i = 0; i < H; ++i) {
+            float t = (xr[i] - mean) * inv;
+            y[m * H + i] = t * w[i] + b[i];
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Attention — flash_attn_ext with K/V cast to fp16 and F32 precision        */
+/* (siglip2_vision.cpp:154-175), kq_scale = 1/sqrt(d_head) (:629-632).       */
+/* ------------------------------------------------------------------------ */
+void orc_attention(const float *qkv, int64_t T, int64_t H, int64_t n_head,
+                   const int64_t *seq_off, const int64_t *seq_len, int64_t n_seq,
+                   float *out) {
+    (void) T;
+    const int64_t dh = H / n_head;
+    const float scale = 1.0f / sqrtf((float) dh);
+    const int64_t ld = 3 * H;
+    for (int64_t s = 0; s < n_seq; ++s) {
+        const int64_t off = seq_off[s], L = seq_len[s];
+        float *kh = (float *) malloc((size_t) L * (size_t) H * sizeof(float));
+        float *vh = (float *) malloc((size_t) L * (size_t) H * sizeof(float));
+        for (int64_t t = 0; t < L; ++t)
+            for (int64_t i = 0; i < H; ++i) {
+                kh[t * H + i] = orc_fp16_to_fp32(orc_fp32_to_fp16(qkv[(off + t) * ld + H + i]));
+                vh[t * H + i] = orc_fp16_to_fp32(orc_fp32_to_fp16(qkv[(off + t) * ld + 2 * H + i]));
+            }
+        #pragma omp parallel for schedule(static) collapse(2)
+        for (int64_t hd = 0; hd < n_head; ++hd) {
+            for (int64_t q = 0; q < L; ++q) {
+                const float *qr = qkv + (off + q) * ld + hd * dh;
+                double *sc = (double *) malloc((size_t) L * sizeof(double));
+                double mx = -INFINITY;
+                for (int64_t k = 0; k < L; ++k) {
+                    const float *kr = kh + k * H + hd * dh;
+                    double dot = 0.0;
+                    for (int64_t i = 0; i < dh; ++i) dot += (double) qr[i] * (double) kr[i];
+                    sc[k] = dot * (double) scale;
+                    if (sc[k] > mx) mx = sc[k];
+                }
+                double den = 0.0;
+                for (int64_t k = 0; k < L; ++k) { sc[k] = exp(sc[k] - mx); den += sc[k]; }
+                for (int64_t i = 0; i < dh; ++i) {
+                    double acc = 0.0;
+                    for (int64_t k = 0; k < L; ++k) acc += sc[k] * (double) vh[k * H + hd * dh + i];
+                    out[(off + q) * H + hd * dh + i] = (float) (acc / den);
+                }
+                free(sc);
+            }
+        }
+        free(kh);
+        free(vh);
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Position-embedding resize: bilinear with antialias, align_corners=False  */
+/* (ggml_interpolate BILINEAR|ANTIALIAS at siglip2_vision.cpp:680-691, the   */
+/* counterpart of HF's F.interpolate(..., antialias=True)).  Separable       */
+/* triangle filter of support max(1, in/out), weights normalised per output. */
+/* Width pass first, then height.                                            */
+/* ------------------------------------------------------------------------ */
+static void aa_weights(int64_t in, int64_t out, int64_t i, int64_t *lo, int64_t *cnt, double *wt) {
+    double scale = (double) in / (double) out;
+    double support = scale >= 1.0 ? scale : 1.0;
+    double center = scale * ((double) i + 0.5);
+    double invs = scale >= 1.0 ? 1.0 / scale : 1.0;
+    int64_t xmin = (int64_t) (center - support + 0.5);
+    if (xmin < 0) xmin = 0;
+    int64_t xmax = (int64_t) (center + support + 0.5);
+    if (xmax > in) xmax = in;
+    double tot = 0.0;
+    int64_t n = xmax - xmin;
+    for (int64_t j = 0; j < n; ++j) {
+        double a = ((double) (j + xmin) - center + 0.5) * invs;
+        double w = 1.0 - fabs(a);
+        if (w < 0.0) w = 0.0;
+        wt[j] = w;
+        tot += w;
+    }
+    for (int64_t j = 0; j < n; ++j) wt[j] = tot != 0.0 ? wt[j] / tot : 0.0;
+    *lo = xmin;
+    *cnt = n;
+}
+
+void orc_pos_resize(const float *table, int64_t side, int64_t H,
+                    int64_t h, int64_t w, float *out) {
+    /* tmp: [side][w][H] */
+    float *tmp = (float *) malloc((size_t) side * (size_t) w * (size_t) H * sizeof(float));
+    double wt[256];
+    for (int64_t c = 0; c < w; ++c) {
+        int64_t lo, n;
+        aa_weights(side, w, c, &lo, &n, wt);
+        for (int64_t r = 0; r < side; ++r)
+            for (int64_t i = 0; i < H; ++i) {
+                double acc = 0.0;
+                for (int64_t j = 0; j < n; ++j) acc += wt[j] * (double) table[(r * side + lo + j) * H + i];
+                tmp[(r * w + c) * H + i] = (float) acc;
+            }
+    }
+    for (int64_t r = 0; r < h; ++r) {
+        int64_t lo, n;
+        aa_weights(side, h, r, &lo, &n, wt);
+        for (int64_t c = 0; c < w; ++c)
+            for (int64_t i = 0; i < H; ++i) {
+                double acc = 0.0;
+                for (int64_t j = 0; j < n; ++j) acc += wt[j] * (double) tmp[((lo + j) * w + c) * H + i];
+                out[(r * w + c) * H + i] = (float) acc;
+            }
+    }
+    free(tmp);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Towers                                                                    */
+/* ------------------------------------------------------------------------ */
+
+/* y[M][N] = X[M][K] @ W^T (+ epilogue) with the q8_1 activation rule, or in  */
+/* fp32 against dequantized weights when quant_act == 0.                     */
+static void proj(const uint8_t *w, int64_t N, int64_t K, int64_t Kp, const float *x, int64_t M,
+                 int quant_act, float *y) {
+    if (quant_act) {
+        int8_t *qs = (int8_t *) malloc((size_t) M * (size_t) Kp);
+        float  *dx = (float *) malloc((size_t) M * (size_t) (Kp / 32) * sizeof(float));
+        orc_quantize_q8_1(x, M, K, K, Kp, qs, dx);
+        orc_gemm_q8(w, N, Kp, qs, dx, M, y, NULL);
+        free(qs);
+        free(dx);
+    } else {
+        float *wf = (float *) malloc((size_t) N * (size_t) Kp * sizeof(float));
+        orc_dequantize_q8_0(w, N, Kp, wf);
+        #pragma omp parallel for schedule(static)
+        for (int64_t m = 0; m < M; ++m)
+            for (int64_t n = 0; n < N; ++n) {
+                double acc = 0.0;
+                for (int64_t k = 0; k < K; ++k) acc += (double) x[m * K + k] * (double) wf[n * Kp + k];
+                y[m * N + n] = (float) acc;
+            }
+        free(wf);
+    }
+}
+
+static void add_bias(float *y, const float *b, int64_t M, int64_t N) {
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t n = 0; n < N; ++n) y[m * N + n] = y[m * N + n] + b[n];
+}
+
+/* one pre-LN encoder block (siglip2_vision.cpp:181-244; siglip2_text.cpp:216-302) */
+static void encoder_block(const orc_block *B, float *x, int64_t T, int64_t H, int64_t F, int64_t Fp,
+                          int64_t n_head, float eps, const int64_t *seq_off, const int64_t *seq_len,
+                          int64_t n_seq, int quant_act) {
+    float *ln  = (float *) malloc((size_t) T * H * sizeof(float));
+    float *qkv = (float *) malloc((size_t) T * 3 * H * sizeof(float));
+    float *att = (float *) malloc((size_t) T * H * sizeof(float));
+    float *o   = (float *) malloc((size_t) T * H * sizeof(float));
+    float *up  = (float *) malloc((size_t) T * F * sizeof(float));
+
+    orc_layernorm(x, B->ln1_w, B->ln1_b, eps, T, H, ln);
+    proj(B->qkv_w, 3 * H, H, H, ln, T, quant_act, qkv);
+    add_bias(qkv, B->qkv_b, T, 3 * H);
+    orc_attention(qkv, T, H, n_head, seq_off, seq_len, n_seq, att);
+    proj(B->o_w, H, H, H, att, T, quant_act, o);
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t i = 0; i < H; ++i)
+            x[t * H + i] = (o[t * H + i] + B->o_b[i]) + x[t * H + i];
+
+    orc_layernorm(x, B->ln2_w, B->ln2_b, eps, T, H, ln);
+    proj(B->up_w, F, H, H, ln, T, quant_act, up);
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t i = 0; i < F; ++i)
+            up[t * F + i] = orc_gelu(up[t * F + i] + B->up_b[i]);
+    proj(B->down_w, H, F, Fp, up, T, quant_act, o);
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t i = 0; i < H; ++i)
+            x[t * H + i] = (o[t * H + i] + B->down_b[i]) + x[t * H + i];
+
+    free(ln); free(qkv); free(att); free(o); free(up);
+}
+
+int orc_vision_encode(const orc_vision_weights *W, const float *patches,
+                      int64_t h, int64_t w, int pooling, int quant_act, float *out) {
+    const int64_t H = W->H, T = h * w;
+    float *x   = (float *) malloc((size_t) T * H * sizeof(float));
+    float *pos = (float *) malloc((size_t) T * H * sizeof(float));
+
+    /* patch embed + bias, then + resized position table (siglip2_vision.cpp:676-691) */
+    proj(W->patch_w, H, W->patch_dim, W->patch_dim, patches, T, quant_act, x);
+    if (h == W->pos_side && w == W->pos_side)
+        memcpy(pos, W->pos_embd, (size_t) T * H * sizeof(float));
+    else
+        orc_pos_resize(W->pos_embd, W->pos_side, H, h, w, pos);
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t i = 0; i < H; ++i)
+            x[t * H + i] = (x[t * H + i] + W->patch_b[i]) + pos[t * H + i];
+
+    int64_t so = 0, sl = T;
+    for (int64_t l = 0; l < W->n_layer; ++l)
+        encoder_block(&W->blocks[l], x, T, H, W->F, W->Fp, W->n_head, W->eps, &so, &sl, 1, quant_act);
+
+    orc_layernorm(x, W->post_ln_w, W->post_ln_b, W->eps, T, H, x);
+
+    if (pooling == 0) {
+        /* MEAN (siglip2_vision.cpp:699-701) */
+        for (int64_t i = 0; i < H; ++i) {
+            double acc = 0.0;
+            for (int64_t t = 0; t < T; ++t) acc += x[t * H + i];
+            out[i] = (float) (acc / (double) T);
+        }
+    } else {
+        /* attention-pool head (siglip2_vision.cpp:249-314) */
+        float *q   = (float *) malloc((size_t) H * sizeof(float));
+        float *qkv = (float *) malloc((size_t) (T + 1) * 3 * H * sizeof(float));
+        float *k   = (float *) malloc((size_t) T * H * sizeof(float));
+        float *v   = (float *) malloc((size_t) T * H * sizeof(float));
+        float *att = (float *) malloc((size_t) (T + 1) * H * sizeof(float));
+        float *a   = (float *) malloc((size_t) H * sizeof(float));
+        float *n1  = (float *) malloc((size_t) H * sizeof(float));
+        float *up  = (float *) malloc((size_t) W->F * sizeof(float));
+        float *dn  = (float *) malloc((size_t) H * sizeof(float));
+        proj(W->hq_w, H, H, H, W->probe, 1, quant_act, q);
+        add_bias(q, W->hq_b, 1, H);
+        proj(W->hk_w, H, H, H, x, T, quant_act, k);
+        add_bias(k, W->hk_b, T, H);
+        proj(W->hv_w, H, H, H, x, T, quant_act, v);
+        add_bias(v, W->hv_b, T, H);
+        /* pack [probe q ; K ; V] rows: query row 0 attends to key rows 1..T */
+        memset(qkv, 0, (size_t) (T + 1) * 3 * H * sizeof(float));
+        memcpy(qkv, q, (size_t) H * sizeof(float));
+        for (int64_t t = 0; t < T; ++t) {
+            memcpy(qkv + (t + 1) * 3 * H + H, k + t * H, (size_t) H * sizeof(float));
+            memcpy(qkv + (t + 1) * 3 * H + 2 * H, v + t * H, (size_t) H * sizeof(float));
+        }
+        /* single query against T keys: attention over rows 1..T with query row 0 */
+        {
+            const int64_t dh = H / W->n_head;
+            const float scale = 1.0f / sqrtf((float) dh);
+            for (int64_t hd = 0; hd < W->n_head; ++hd) {
+                double *sc = (double *) malloc((size_t) T * sizeof(double));
+                double mx = -INFINITY;
+                for (int64_t t = 0; t < T; ++t) {
+                    double dot = 0.0;
+                    for (int64_t i = 0; i < dh; ++i) {
+                        float kv = orc_fp16_to_fp32(orc_fp32_to_fp16(k[t * H + hd * dh + i]));
+                        dot += (double) q[hd * dh + i] * (double) kv;
+                    }
+                    sc[t] = dot * (double) scale;
+                    if (sc[t] > mx) mx = sc[t];
+                }
+                double den = 0.0;
+                for (int64_t t = 0; t < T; ++t) { sc[t] = exp(sc[t] - mx); den += sc[t]; }
+                for (int64_t i = 0; i < dh; ++i) {
+                    double acc = 0.0;
+                    for (int64_t t = 0; t < T; ++t)
+                        acc += sc[t] * (double) orc_fp16_to_fp32(orc_fp32_to_fp16(v[t * H + hd * dh + i]));
+                    att[hd * dh + i] = (float) (acc / den);
+                }
+                free(sc);
+            }
+        }
+        proj(W->ho_w, H, H, H, att, 1, quant_act, a);
+        add_bias(a, W->ho_b, 1, H);
+        orc_layernorm(a, W->hln_w, W->hln_b, W->eps, 1, H, n1);
+        proj(W->hup_w, W->F, H, H, n1, 1, quant_act, up);
+        for (int64_t i = 0; i < W->F; ++i) up[i] = orc_gelu(up[i] + W->hup_b[i]);
+        proj(W->hdown_w, H, W->F, W->Fp, up, 1, quant_act, dn);
+        for (int64_t i = 0; i < H; ++i) out[i] = a[i] + (dn[i] + W->hdown_b[i]);
+        free(q); free(qkv); free(k); free(v); free(att); free(a); free(n1); free(up); free(dn);
+    }
+    free(x);
+    free(pos);
+    return 0;
+}
+
+int orc_text_encode(const orc_text_weights *W, const int32_t *ids, int64_t n_prompts,
+                    int quant_act, float *out) {
+    const int64_t H = W->H, P = W->n_pos, T = n_prompts * P;
+    const int64_t Kb = H / 32;
+    float *x = (float *) malloc((size_t) T * H * sizeof(float));
+    /* get_rows(token_embd Q8_0) dequantizes the row; + position row (siglip2_text.cpp:837-847) */
+    for (int64_t t = 0; t < T; ++t) {
+        int64_t id = ids[t];
+        const uint8_t *row = W->tok_embd + id * Kb * 34;
+        for (int64_t kb = 0; kb < Kb; ++kb) {
+            uint16_t dh;
+            memcpy(&dh, row + kb * 34, 2);
+            float d = orc_fp16_to_fp32(dh);
+            for (int j = 0; j < 32; ++j) {
+                float e = (float) (int8_t) row[kb * 34 + 2 + j] * d;
+                x[t * H + kb * 32 + j] = e + W->pos_embd[(t % P) * H + kb * 32 + j];
+            }
+        }
+    }
+    int64_t *so = (int64_t *) malloc((size_t) n_prompts * sizeof(int64_t));
+    int64_t *sl = (int64_t *) malloc((size_t) n_prompts * sizeof(int64_t));
+    for (int64_t p = 0; p < n_prompts; ++p) { so[p] = p * P; sl[p] = P; }
+    for (int64_t l = 0; l < W->n_layer; ++l)
+        encoder_block(&W->blocks[l], x, T, H, W->F, W->Fp, W->n_head, W->eps, so, sl, n_prompts, quant_act);
+    orc_layernorm(x, W->final_ln_w, W->final_ln_b, W->eps, T, H, x);
+    /* last-token pool (pool_idx = n_pos-1) then head (siglip2_text.cpp:857-865) */
+    float *pooled = (float *) malloc((size_t) n_prompts * H * sizeof(float));
+    for (int64_t p = 0; p < n_prompts; ++p)
+        memcpy(pooled + p * H, x + (p * P + P - 1) * H, (size_t) H * sizeof(float));
+    proj(W->head_w, H, H, H, pooled, n_prompts, quant_act, out);
+    add_bias(out, W->head_b, n_prompts, H);
+    free(x); free(so); free(sl); free(pooled);
+    return 0;
+}
+
+void orc_score(const float *img, int64_t I, const float *txt, int64_t J, int64_t H,
+               float logit_scale, float logit_bias, float *out) {
+    float *a = (float *) malloc((size_t) I * H * sizeof(float));
+    float *b = (float *) malloc((size_t) J * H * sizeof(float));
+    memcpy(a, img, (size_t) I * H * sizeof(float));
+    memcpy(b, txt, (size_t) J * H * sizeof(float));
+    float *rows[2] = { a, b };
+    int64_t nr[2] = { I, J };
+    for (int s = 0; s < 2; ++s)
+        for (int64_t r = 0; r < nr[s]; ++r) {
+            float *row = rows[s] + r * H;
+            double sumsq = 0.0;
+            for (int64_t c = 0; c < H; ++c) sumsq += (double) row[c] * (double) row[c];
+            float inv = (float) (1.0 / (sqrt(sumsq) + 1e-12));
+            for (int64_t c = 0; c < H; ++c) row[c] *= inv;
+        }
+    const float scale = expf(logit_scale);
+    #pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < I; ++i)
+        for (int64_t j = 0; j < J; ++j) {
+            double dot = 0.0;
+            for (int64_t c = 0; c < H; ++c) dot += (double) a[i * H + c] * (double) b[j * H + c];
+            float logit = (float) (dot * (double) scale + (double) logit_bias);
+            float p;
+            if (logit >= 0.0f) { float e = expf(-logit); p = 1.0f / (1.0f + e); }
+            else               { float e = expf(logit);  p = e / (1.0f + e); }
+            out[i * J + j] = p;
+        }
+    free(a);
+    free(b);
+}
