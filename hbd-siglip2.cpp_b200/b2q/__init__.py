@@ -1,0 +1,186 @@
+"""Python binding of libb2q.so (include/b2q.h) — the host side used by tests
+and benchmarks.  Device buffers are torch CUDA tensors (torch is plumbing
+here: memory, streams, process groups); every computation goes through the
+C ABI.  There is no fallback: if the library is missing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parents[1]
+LIB_PATH = PKG / "lib" / "libb2q.so"
+
+OK = 0
+ERR_INVALID, ERR_SHAPE, ERR_ALIGN, ERR_CUDA, ERR_DEVICE, ERR_NOT_INIT, ERR_NOMEM = -1, -2, -3, -4, -5, -6, -7
+OPS_I8, OPS_F16 = 0, 1
+EPI_NONE, EPI_BIAS, EPI_BIAS_RESIDUAL, EPI_BIAS_GELU_Q8, EPI_BIAS_F16 = 0, 1, 2, 3, 4
+
+#: every symbol include/b2q.h declares (checked by the CPU test suite)
+EXPORTS = [
+    "b2q_last_error", "b2q_abi_version", "b2q_init", "b2q_tune", "b2q_check_device",
+    "b2q_weight_register", "b2q_weight_release", "b2q_weight_shape",
+    "b2q_act_bytes", "b2q_act_layout", "b2q_quantize_q8_1", "b2q_ln_quantize_q8_1",
+    "b2q_mul_mat_q8_0", "b2q_mul_mat_q8_0_f32", "b2q_block_sums",
+]
+
+
+class B2QError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"b2q status {status}: {msg}")
+        self.status = status
+
+
+class Epilogue(C.Structure):
+    _fields_ = [("kind", C.c_int), ("bias", C.c_void_p), ("residual", C.c_void_p),
+                ("act_out", C.c_void_p), ("ld_out", C.c_int64)]
+
+
+_lib = None
+P, I64 = C.c_void_p, C.c_int64
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: run __graft_entry__.build() (no CPU fallback exists)")
+        L = C.CDLL(str(LIB_PATH))
+        L.b2q_last_error.restype = C.c_char_p
+        L.b2q_abi_version.restype = C.c_int
+        L.b2q_init.argtypes = [C.c_int, C.c_int]
+        L.b2q_check_device.argtypes = [P, C.POINTER(C.c_uint32)]
+        L.b2q_tune.argtypes = [C.c_int, I64]
+        L.b2q_weight_register.argtypes = [P, I64, I64, I64, C.c_int, P, C.POINTER(P)]
+        L.b2q_weight_release.argtypes = [P]
+        L.b2q_weight_shape.argtypes = [P, C.POINTER(I64), C.POINTER(I64)]
+        L.b2q_act_bytes.argtypes = [I64, I64]
+        L.b2q_act_bytes.restype = C.c_size_t
+        L.b2q_act_layout.argtypes = [I64, I64] + [C.POINTER(I64)] * 4
+        L.b2q_quantize_q8_1.argtypes = [P, I64, I64, I64, P, P]
+        L.b2q_ln_quantize_q8_1.argtypes = [P, P, P, C.c_float, I64, I64, P, P, P]
+        L.b2q_mul_mat_q8_0.argtypes = [P, P, I64, P, C.POINTER(Epilogue), P]
+        L.b2q_mul_mat_q8_0_f32.argtypes = [P, P, I64, I64, P, P, P]
+        L.b2q_block_sums.argtypes = [P, P, I64, P, P]
+        for name in EXPORTS:
+            fn = getattr(L, name)
+            if name not in ("b2q_last_error", "b2q_abi_version", "b2q_act_bytes"):
+                fn.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def check(status: int):
+    if status != OK:
+        raise B2QError(status, lib().b2q_last_error().decode())
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def init(device: int = 0, ops_mode: int = -1):
+    check(lib().b2q_init(device, ops_mode))
+
+
+TUNE_GEMM_BN, TUNE_TIMEOUT_NS = 1, 2
+
+
+def tune(key: int, value: int):
+    check(lib().b2q_tune(key, value))
+
+
+def check_device(stream=None) -> int:
+    code = C.c_uint32(0)
+    check(lib().b2q_check_device(_stream(stream), C.byref(code)))
+    return code.value
+
+
+class Weight:
+    """A registered Q8_0 weight (N rows of K; K-padded tensors pass padded K)."""
+
+    def __init__(self, q8_0, n: int, k: int, row_bytes: int | None = None, stream=None):
+        import torch
+        row_bytes = row_bytes or (k // 32 * 34)
+        handle = C.c_void_p()
+        if isinstance(q8_0, np.ndarray):
+            buf = np.ascontiguousarray(q8_0)
+            check(lib().b2q_weight_register(buf.ctypes.data, n, k, row_bytes, 1, _stream(stream), C.byref(handle)))
+        else:
+            assert isinstance(q8_0, torch.Tensor) and q8_0.is_cuda
+            check(lib().b2q_weight_register(q8_0.data_ptr(), n, k, row_bytes, 0, _stream(stream), C.byref(handle)))
+        self.handle = handle
+        self.n, self.k = n, k
+
+    def release(self):
+        if self.handle:
+            lib().b2q_weight_release(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+def act_layout(m: int, k: int):
+    kp, es, off, ld = I64(), I64(), I64(), I64()
+    check(lib().b2q_act_layout(m, k, C.byref(kp), C.byref(es), C.byref(off), C.byref(ld)))
+    return kp.value, es.value, off.value, ld.value
+
+
+def act_empty(m: int, k: int):
+    """Allocate an activation buffer (uint8 torch tensor, 256-byte aligned)."""
+    import torch
+    nbytes = int(lib().b2q_act_bytes(m, k))
+    if nbytes == 0:
+        raise B2QError(ERR_SHAPE, "bad activation shape")
+    t = torch.empty(nbytes + 256, dtype=torch.uint8, device="cuda")
+    off = (-t.data_ptr()) % 256
+    return t[off:off + nbytes]
+
+
+def act_planes(act, m: int, k: int):
+    """Decode an activation buffer -> (int8 values [M][Kp], fp32 scales [M][Kb]) as torch tensors."""
+    import torch
+    kp, es, off, ld = act_layout(m, k)
+    if es == 1:
+        q = act[: m * kp].view(torch.int8).view(m, kp)
+    else:
+        q = act[: m * kp * 2].view(torch.float16).view(m, kp).to(torch.int8)
+    d = act[off: off + (kp // 32) * ld * 4].view(torch.float32).view(kp // 32, ld)[:, :m].t()
+    return q, d
+
+
+def quantize_q8_1(x, act, m: int, k: int, ldx: int | None = None, stream=None):
+    check(lib().b2q_quantize_q8_1(_ptr(x), m, k, ldx or k, _ptr(act), _stream(stream)))
+
+
+def ln_quantize(x, w, b, eps: float, m: int, h: int, act, y=None, stream=None):
+    check(lib().b2q_ln_quantize_q8_1(_ptr(x), _ptr(w), _ptr(b), eps, m, h, _ptr(act), _ptr(y), _stream(stream)))
+
+
+def mul_mat(w: Weight, act, m: int, y=None, kind: int = EPI_NONE, bias=None, residual=None, act_out=None,
+            ld_out: int = 0, stream=None):
+    e = Epilogue(kind, _ptr(bias), _ptr(residual), _ptr(act_out), ld_out)
+    check(lib().b2q_mul_mat_q8_0(w.handle, _ptr(act), m, _ptr(y), C.byref(e), _stream(stream)))
+
+
+def mul_mat_f32(w: Weight, x, m: int, x_cols: int, y, scratch, stream=None):
+    check(lib().b2q_mul_mat_q8_0_f32(w.handle, _ptr(x), m, x_cols, _ptr(y), _ptr(scratch), _stream(stream)))
+
+
+def block_sums(w: Weight, act, m: int, out, stream=None):
+    check(lib().b2q_block_sums(w.handle, _ptr(act), m, _ptr(out), _stream(stream)))

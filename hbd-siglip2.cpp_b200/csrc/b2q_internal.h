@@ -1,0 +1,82 @@
+// b2q_internal.h — host-side declarations shared by the library's .cu files.
+#pragma once
+
+#include <cstdint>
+#include <cstddef>
+#include <string>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/b2q.h"
+
+namespace b2q {
+
+// Operand carriers for the int8 values fed to the tensor cores.
+enum OpsMode : int { kOpsI8 = 0, kOpsF16 = 1 };
+
+inline int ops_elem_bytes(int mode) { return mode == kOpsF16 ? 2 : 1; }
+inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// Activation buffer layout ("q8_1 planes"): for M rows of logical width K,
+// Kp = round_up(K, 32), Kb = Kp / 32:
+//   qs : [M][Kp] int8 values (1 byte each, or fp16 carriers in F16 mode)
+//   d  : [Kb][ld] fp32 per-block scales, ld = round_up(M, 4), at byte offset
+//        round_up(M*Kp*es, 256)
+struct ActLayout {
+    int64_t M, K, Kp, Kb, ld, es;
+    size_t d_offset, bytes;
+};
+ActLayout act_layout(int64_t M, int64_t K, int mode);
+
+struct DeviceState {
+    int device = -1;
+    int num_sms = 0;
+    int mode = kOpsF16;
+    uint32_t* err = nullptr;      // device error word (cudaMalloc'ed at init)
+    uint64_t timeout_ns = 2000000000ull;
+    int gemm_bn = 0;              // GEMM tile width: 128, 256, or 0 = by shape
+};
+DeviceState* state();             // per-thread current device state
+b2q_status set_error(b2q_status st, const std::string& msg);
+b2q_status cuda_check(cudaError_t e, const char* what);
+
+// TMA descriptor creation through the driver entry point.
+bool make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+
+}  // namespace b2q
+
+// Registered weight: repacked planes of a ggml Q8_0 tensor (N rows of K).
+struct b2q_weight {
+    int64_t N = 0, K = 0, Kb = 0;
+    int mode = 0;
+    int device = -1;
+    void* q = nullptr;     // [N][K] int8 (or fp16 carriers)
+    float* d = nullptr;    // [Kb][N] fp32 (exact widening of the fp16 scales)
+    CUtensorMap tm_q256, tm_q128;   // box 128 B x {256,128} rows, 128-byte swizzle
+    CUtensorMap tm_d256, tm_d128;   // box {256,128} x (scales per stage)
+};
+
+namespace b2q {
+// kernels (launchers return cudaError_t of the launch)
+cudaError_t launch_repack_q8_0(const void* raw, int64_t N, int64_t Kb, int64_t row_bytes, int mode, void* q,
+                               float* d, cudaStream_t s);
+cudaError_t launch_quantize_q8_1(const float* x, int64_t M, int64_t K, int64_t ldx, void* act, int mode,
+                                 cudaStream_t s);
+cudaError_t launch_ln_quant(const float* x, const float* w, const float* b, float eps, int64_t M, int64_t H,
+                            void* act, float* y, int mode, cudaStream_t s);
+
+struct GemmArgs {
+    const b2q_weight* w;
+    const void* act;
+    int64_t M;
+    int epi;
+    const float* bias;
+    const float* residual;
+    void* out;
+    int64_t ld_out;
+    void* act_out;          // GELU_Q8 destination (activation buffer, K' = N)
+    int32_t* dump;          // block sums [Kb][M][N] (debug)
+};
+b2q_status launch_gemm(const GemmArgs& a, cudaStream_t s);
+}  // namespace b2q

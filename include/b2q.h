@@ -1,0 +1,135 @@
+/*
+ * b2q.h — C ABI of the B200 (sm_100a) SigLIP2 Q8_0 x q8_1 hot path.
+ *
+ * Plain pointers and sizes only.  Device pointers are CUDA device addresses
+ * on the calling thread's current device; `stream` is a cudaStream_t (NULL =
+ * legacy default stream).  Every call returns a b2q_status (0 = OK); on
+ * failure b2q_last_error() describes it.  No call traps or aborts, and no
+ * launch call allocates device memory, so launches can be captured into CUDA
+ * graphs (pointers are baked into the graph, as in the reference).
+ *
+ * Reference interfaces replaced (paths inside the hbd-siglip2.cpp project):
+ *  - ggml_mul_mat(W Q8_0, X F32) executed by ggml-cuda's MMQ — call sites
+ *    src/siglip2_vision.cpp:199,227,235,239,676 and src/siglip2_text.cpp:189,
+ *    196,200,864; raw-pointer precedent src/cuda/siglip2_custom_mmq.cuh:96-103
+ *  - quantize_q8_1 (src/cuda/siglip2_custom_mmq.cuh:63-67)
+ *  - fused LayerNorm (src/cuda/siglip2_megakernel.cuh:49-57)
+ *  - the bias+GELU / bias+residual tails (src/cuda/siglip2_megakernel.cuh:
+ *    126-142) — here folded into the GEMM epilogue.
+ */
+#ifndef B2Q_H
+#define B2Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int b2q_status;
+enum {
+    B2Q_OK = 0,
+    B2Q_ERR_INVALID = -1,   /* null pointer, unknown enum value           */
+    B2Q_ERR_SHAPE = -2,     /* unsupported or inconsistent shape          */
+    B2Q_ERR_ALIGN = -3,     /* pointer or stride alignment                 */
+    B2Q_ERR_CUDA = -4,      /* CUDA runtime / driver error                 */
+    B2Q_ERR_DEVICE = -5,    /* a kernel's bounded wait expired             */
+    B2Q_ERR_NOT_INIT = -6,  /* b2q_init not called on this thread/device   */
+    B2Q_ERR_NOMEM = -7      /* allocation at init/registration failed      */
+};
+
+/* Operand carrier of the int8 values on the tensor cores. */
+enum {
+    B2Q_OPS_I8 = 0,   /* tcgen05 kind::i8, int32 accumulators              */
+    B2Q_OPS_F16 = 1   /* int8 values carried exactly in fp16, kind::f16    */
+};
+
+/* Thread-local description of the last failure on this thread. */
+const char *b2q_last_error(void);
+int b2q_abi_version(void);
+
+/* Per-device set-up (current device); allocates the device error word.
+ * ops_mode: B2Q_OPS_I8 or B2Q_OPS_F16 (-1 = library default). */
+b2q_status b2q_init(int device, int ops_mode);
+/* Tuning knobs of the current device's state (reference precedent: the
+ * SIGLIP2_* environment switches of src/cuda/siglip2_megakernel.cu:1378-1401).
+ *   B2Q_TUNE_GEMM_BN:   GEMM tile width 128 or 256 (0 = chosen per shape)
+ *   B2Q_TUNE_TIMEOUT_NS: bound of every in-kernel wait (default 2 s) */
+enum { B2Q_TUNE_GEMM_BN = 1, B2Q_TUNE_TIMEOUT_NS = 2 };
+b2q_status b2q_tune(int key, int64_t value);
+/* Reads (and clears) the device error word after synchronising `stream`. */
+b2q_status b2q_check_device(void *stream, uint32_t *code_out);
+
+/* ---- weights -------------------------------------------------------------
+ * Registers a ggml Q8_0 tensor (block_q8_0 = fp16 d + 32 int8, 34 bytes):
+ * N rows of K (ne[0], a multiple of 32; K-padded tensors pass the padded K),
+ * row stride row_bytes (>= K/32*34).  `q8_0` is a device pointer, or a host
+ * pointer when src_is_host != 0.  Repacks once into a 16-byte-aligned value
+ * plane [N][K] and a scale plane [K/32][N]; the source is not retained.
+ * Replaces the per-call raw read in src/cuda/siglip2_custom_mmq.cu:176-199. */
+typedef struct b2q_weight b2q_weight;
+b2q_status b2q_weight_register(const void *q8_0, int64_t N, int64_t K, int64_t row_bytes, int src_is_host,
+                               void *stream, b2q_weight **out);
+b2q_status b2q_weight_release(b2q_weight *w);
+b2q_status b2q_weight_shape(const b2q_weight *w, int64_t *N, int64_t *K);
+
+/* ---- activations ("q8_1 planes") -----------------------------------------
+ * An activation buffer holds M rows of logical width K quantized per 32
+ * columns (Kp = K rounded up to 32; columns K..Kp-1 are zero, the pad_x_to_w
+ * rule of src/siglip2_vision.cpp:99-107):
+ *   values: [M][Kp], 1 byte each (B2Q_OPS_I8) or fp16 carriers (B2Q_OPS_F16)
+ *   scales: [Kp/32][ld] fp32, ld = M rounded up to 4, at byte offset
+ *           scale_offset (256-aligned)
+ * The caller allocates b2q_act_bytes(M, K) bytes (256-byte aligned). */
+size_t b2q_act_bytes(int64_t M, int64_t K);
+b2q_status b2q_act_layout(int64_t M, int64_t K, int64_t *Kp, int64_t *value_bytes, int64_t *scale_offset,
+                          int64_t *scale_ld);
+
+/* q8_1 quantize of fp32 rows x[M][ldx] (src/cuda/siglip2_custom_mmq.cu:51-97):
+ * d = max|x|/127, q = rint(x*127/max|x|). */
+b2q_status b2q_quantize_q8_1(const float *x, int64_t M, int64_t K, int64_t ldx, void *act, void *stream);
+
+/* LayerNorm + affine then q8_1 quantize of the result, one pass
+ * (src/cuda/siglip2_megakernel.cu:81-138 fused with the quantize step that
+ * feeds the next mul_mat).  H must be a multiple of 128.  y_opt (may be
+ * NULL) also receives the fp32 LayerNorm output. */
+b2q_status b2q_ln_quantize_q8_1(const float *x, const float *w, const float *b, float eps, int64_t M, int64_t H,
+                                void *act, float *y_opt, void *stream);
+
+/* ---- GEMM ------------------------------------------------------------------
+ * y[m][n] = sum_kb dW[n,kb] * dX[m,kb] * S[m,n,kb], S the int32 dot of the
+ * 32 int8 pairs of block kb, accumulated in fp32 over ascending kb as
+ * fma((float)S*dW, dX, acc) (src/cuda/siglip2_custom_mmq.cu:263-266),
+ * followed by the epilogue below.  Output row stride ld_out (0 = N). */
+enum {
+    B2Q_EPI_NONE = 0,            /* y = acc                                  fp32  */
+    B2Q_EPI_BIAS = 1,            /* y = acc + bias                           fp32  */
+    B2Q_EPI_BIAS_RESIDUAL = 2,   /* y = (acc + bias) + residual              fp32  */
+    B2Q_EPI_BIAS_GELU_Q8 = 3,    /* act_out <- q8_1(gelu(acc + bias)), K'=N        */
+    B2Q_EPI_BIAS_F16 = 4         /* y = fp16(acc + bias)                     fp16  */
+};
+typedef struct b2q_epilogue {
+    int kind;
+    const float *bias;      /* [N] or NULL (treated as zeros)                 */
+    const float *residual;  /* [M][ld_out] for BIAS_RESIDUAL; may equal y     */
+    void *act_out;          /* activation buffer (M rows, K' = N) for GELU_Q8 */
+    int64_t ld_out;         /* elements; 0 means N                            */
+} b2q_epilogue;
+
+b2q_status b2q_mul_mat_q8_0(const b2q_weight *w, const void *act, int64_t M, void *y, const b2q_epilogue *epi,
+                            void *stream);
+
+/* ggml_mul_mat(W Q8_0, X F32) -> Y F32 [M][N]: quantizes X (K = x_cols <= W's
+ * K, zero-extended) into act_scratch (b2q_act_bytes(M, W's K) bytes), then
+ * runs the GEMM. */
+b2q_status b2q_mul_mat_q8_0_f32(const b2q_weight *w, const float *x, int64_t M, int64_t x_cols, float *y,
+                                void *act_scratch, void *stream);
+
+/* Debug: the int32 block dots S[kb][m][n] (Kb*M*N int32) of one GEMM. */
+b2q_status b2q_block_sums(const b2q_weight *w, const void *act, int64_t M, int32_t *sums, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2Q_H */

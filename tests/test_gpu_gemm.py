@@ -1,0 +1,213 @@
+"""GPU parity of the q8_1 quantizer, the fused LayerNorm->q8_1 kernel and the
+tcgen05 Q8_0 x q8_1 GEMM against the CPU oracle, through the C ABI.
+
+Bar: bit-exact.  The oracle fixes one fp32 operation order for every op
+(b2q_oracle.h) and the CUDA kernels follow it, so int8 planes, scales, int32
+block sums and fp32 outputs must match exactly, in both operand carriers.
+"""
+import numpy as np
+import pytest
+
+import b2q
+from b2q import synth
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module", params=[(b2q.OPS_F16, 0), (b2q.OPS_I8, 0), (b2q.OPS_F16, 128), (b2q.OPS_I8, 256)],
+                ids=["f16-auto", "i8-auto", "f16-bn128", "i8-bn256"])
+def mode(request):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    ops, bn = request.param
+    b2q.init(0, ops)
+    b2q.tune(b2q.TUNE_GEMM_BN, bn)
+    yield ops
+    b2q.tune(b2q.TUNE_GEMM_BN, 0)
+
+
+def rand(shape, seed, scale=1.0):
+    return (np.random.default_rng(seed).standard_normal(shape).astype(np.float32) * scale)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# ---------------------------------------------------------------- quantize
+@pytest.mark.parametrize("M,K", [(1, 32), (7, 768), (129, 1152), (64, 4304), (729, 1152), (33, 100)])
+def test_quantize_q8_1_bit_exact(oracle, mode, M, K):
+    x = rand((M, K), M * 31 + K)
+    x[0, :32] = 0.0                      # an all-zero block
+    qs_ref, d_ref = oracle.quantize_q8_1(x, (K + 31) // 32 * 32)
+    act = b2q.act_empty(M, K)
+    b2q.quantize_q8_1(dev(x), act, M, K)
+    q, d = b2q.act_planes(act, M, K)
+    np.testing.assert_array_equal(q.cpu().numpy(), qs_ref)
+    np.testing.assert_array_equal(d.cpu().numpy(), d_ref)
+    assert b2q.check_device() == 0
+
+
+@pytest.mark.parametrize("M", [1, 31, 32, 33, 729])
+def test_ln_quantize_bit_exact(oracle, mode, M):
+    H = 1152
+    x = rand((M, H), M, 2.0) + 0.5
+    w = 1.0 + rand(H, 1, 0.1)
+    b = rand(H, 2, 0.1)
+    y_ref = oracle.layernorm(x, w, b, 1e-6)
+    qs_ref, d_ref = oracle.quantize_q8_1(y_ref)
+    act = b2q.act_empty(M, H)
+    y = torch.empty((M, H), dtype=torch.float32, device="cuda")
+    b2q.ln_quantize(dev(x), dev(w), dev(b), 1e-6, M, H, act, y)
+    np.testing.assert_array_equal(y.cpu().numpy(), y_ref)
+    q, d = b2q.act_planes(act, M, H)
+    np.testing.assert_array_equal(q.cpu().numpy(), qs_ref)
+    np.testing.assert_array_equal(d.cpu().numpy(), d_ref)
+
+
+# ---------------------------------------------------------------- GEMM
+def make_case(M, N, K, seed, kpad=None):
+    w_f = rand((N, K), seed, 0.02)
+    kp = kpad or K
+    w_q = synth.quantize_q8_0(w_f, kp)
+    x = rand((M, K), seed + 1)
+    return w_q, x, kp
+
+
+def run_gemm(w_q, N, kp, x, K, kind=b2q.EPI_NONE, bias=None, residual=None):
+    M = x.shape[0]
+    W = b2q.Weight(w_q, N, kp)
+    act = b2q.act_empty(M, kp)
+    b2q.quantize_q8_1(dev(x), act, M, K)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda") if residual is None else dev(residual)
+    b2q.mul_mat(W, act, M, y, kind=kind, bias=None if bias is None else dev(bias),
+                residual=y if residual is not None else None)
+    torch.cuda.synchronize()
+    return W, act, y.cpu().numpy()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 16, 32), (7, 80, 1152), (129, 1152, 1152), (300, 3456, 1152),
+                                   (200, 4304, 1152), (64, 1152, 768), (130, 260, 4320), (1, 1152, 1152)])
+def test_gemm_bit_exact(oracle, mode, M, N, K):
+    w_q, x, kp = make_case(M, N, K, M + N + K)
+    qs, dx = oracle.quantize_q8_1(x, kp)
+    y_ref = oracle.gemm_q8(w_q, N, kp, qs, dx)
+    _, _, y = run_gemm(w_q, N, kp, x, K)
+    np.testing.assert_array_equal(y, y_ref)
+    assert b2q.check_device() == 0
+
+
+def test_gemm_k_padded_fc2(oracle, mode):
+    # ffn_down: logical K = 4304, weight padded to 4320 (135 blocks), activation zero-extended
+    M, N, K = 77, 1152, 4304
+    w_q, x, kp = make_case(M, N, K, 9, kpad=4320)
+    qs, dx = oracle.quantize_q8_1(x, kp)
+    y_ref = oracle.gemm_q8(w_q, N, kp, qs, dx)
+    _, _, y = run_gemm(w_q, N, kp, x, K)
+    np.testing.assert_array_equal(y, y_ref)
+
+
+def test_block_sums_bit_exact(oracle, mode):
+    M, N, K = 70, 272, 256
+    w_q, x, kp = make_case(M, N, K, 3)
+    qs, dx = oracle.quantize_q8_1(x, kp)
+    _, bs_ref = oracle.gemm_q8(w_q, N, kp, qs, dx, block_sums=True)
+    W = b2q.Weight(w_q, N, kp)
+    act = b2q.act_empty(M, kp)
+    b2q.quantize_q8_1(dev(x), act, M, K)
+    out = torch.zeros((kp // 32, M, N), dtype=torch.int32, device="cuda")
+    b2q.block_sums(W, act, M, out)
+    np.testing.assert_array_equal(out.cpu().numpy(), bs_ref.transpose(2, 0, 1))
+
+
+def test_epilogue_bias_and_residual(oracle, mode):
+    M, N, K = 150, 1152, 1152
+    w_q, x, kp = make_case(M, N, K, 5)
+    bias = rand(N, 6, 0.1)
+    res = rand((M, N), 7)
+    qs, dx = oracle.quantize_q8_1(x, kp)
+    acc = oracle.gemm_q8(w_q, N, kp, qs, dx)
+    _, _, y = run_gemm(w_q, N, kp, x, K, kind=b2q.EPI_BIAS, bias=bias)
+    np.testing.assert_array_equal(y, acc + bias)
+    _, _, y = run_gemm(w_q, N, kp, x, K, kind=b2q.EPI_BIAS_RESIDUAL, bias=bias, residual=res)
+    np.testing.assert_array_equal(y, (acc + bias) + res)
+
+
+def test_epilogue_gelu_quantize(oracle, mode):
+    # fc1 -> GELU -> q8_1 planes for fc2 (N = 4304 -> K' = 4320 with a zero tail)
+    M, N, K = 140, 4304, 1152
+    w_q, x, kp = make_case(M, N, K, 8)
+    bias = rand(N, 9, 0.1)
+    qs, dx = oracle.quantize_q8_1(x, kp)
+    acc = oracle.gemm_q8(w_q, N, kp, qs, dx)
+    g = oracle.gelu_vec(acc + bias)
+    q_ref, d_ref = oracle.quantize_q8_1(g, 4320)
+    W = b2q.Weight(w_q, N, kp)
+    act = b2q.act_empty(M, kp)
+    b2q.quantize_q8_1(dev(x), act, M, K)
+    out = b2q.act_empty(M, N)
+    b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=dev(bias), act_out=out)
+    q, d = b2q.act_planes(out, M, N)
+    np.testing.assert_array_equal(q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(d.cpu().numpy(), d_ref)
+
+
+def test_epilogue_f16(oracle, mode):
+    M, N, K = 90, 3456, 1152
+    w_q, x, kp = make_case(M, N, K, 10)
+    bias = rand(N, 11, 0.1)
+    qs, dx = oracle.quantize_q8_1(x, kp)
+    ref = (oracle.gemm_q8(w_q, N, kp, qs, dx) + bias).astype(np.float16)
+    W = b2q.Weight(w_q, N, kp)
+    act = b2q.act_empty(M, kp)
+    b2q.quantize_q8_1(dev(x), act, M, K)
+    y = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    b2q.mul_mat(W, act, M, y, kind=b2q.EPI_BIAS_F16, bias=dev(bias))
+    np.testing.assert_array_equal(y.cpu().numpy(), ref)
+
+
+def test_mul_mat_f32_ggml_semantics(oracle, mode):
+    M, N, K = 33, 1152, 4304
+    w_q, x, kp = make_case(M, N, K, 12, kpad=4320)
+    W = b2q.Weight(w_q, N, kp)
+    scratch = b2q.act_empty(M, kp)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    b2q.mul_mat_f32(W, dev(x), M, K, y, scratch)
+    qs, dx = oracle.quantize_q8_1(x, kp)
+    np.testing.assert_array_equal(y.cpu().numpy(), oracle.gemm_q8(w_q, N, kp, qs, dx))
+
+
+def test_full_size_sampled_rows(oracle, mode):
+    # BASELINE config-2 scale: M = 65536 rows; rows are independent, so the
+    # oracle checks a sample of them bit-exactly.
+    M, N, K = 65536, 4304, 1152
+    w_q = synth.quantize_q8_0(rand((N, K), 21, 0.02))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn((M, K), generator=g, device="cuda")
+    W = b2q.Weight(w_q, N, K)
+    act = b2q.act_empty(M, K)
+    b2q.quantize_q8_1(x, act, M, K)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    b2q.mul_mat(W, act, M, y)
+    torch.cuda.synchronize()
+    assert b2q.check_device() == 0
+    rows = np.concatenate([np.arange(0, 130), np.random.default_rng(0).integers(0, M, 200), np.arange(M - 130, M)])
+    xs = x[torch.from_numpy(rows).cuda()].cpu().numpy()
+    qs, dx = oracle.quantize_q8_1(xs)
+    np.testing.assert_array_equal(y[torch.from_numpy(rows).cuda()].cpu().numpy(), oracle.gemm_q8(w_q, N, K, qs, dx))
+
+
+def test_bad_arguments_return_status(mode):
+    W = b2q.Weight(synth.quantize_q8_0(rand((16, 64), 1)), 16, 64)
+    act = b2q.act_empty(4, 64)
+    with pytest.raises(b2q.B2QError) as e:
+        b2q.mul_mat(W, act[1:], 4, torch.empty((4, 16), device="cuda"))
+    assert e.value.status == b2q.ERR_ALIGN
+    with pytest.raises(b2q.B2QError) as e:
+        b2q.mul_mat(W, act, 4, torch.empty((4, 16), device="cuda"), kind=17)
+    assert e.value.status == b2q.ERR_INVALID
+    with pytest.raises(b2q.B2QError) as e:
+        b2q.Weight(np.zeros((3, 34), np.uint8), 3, 32)
+    assert e.value.status == b2q.ERR_SHAPE
