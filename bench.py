@@ -1,0 +1,342 @@
+#!/usr/bin/env python3
+"""Benchmark: Q8_0 SigLIP2-so400m vision tower, images/s.
+
+One step = one batch of 512 NaFlex images (patch count uniform in [256, 1024]
+on a random grid, patches uniform in [-1, 1], PROBE pooling) through the full
+27-layer Q8_0 tower with synthetic N(0, 0.02) weights, followed by the NCCL
+gather of the 1152-d pooled embeddings to rank 0.  With N GPUs the 512 images
+are sharded across ranks (length-balanced), so total work is fixed: strong
+scaling.  Inputs (1.2 GB of patches) and activations are far larger than L2,
+so no separate L2 flush is needed.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+`value` is device-timed (CUDA events, max over ranks) with patches resident in
+HBM; `e2e` is the same metric through the public host-buffer entry point
+(b2q_vision_encode_host: pinned host patches in, host embeddings out) plus the
+gather.  `roofline` is the dominant kernel, the fc1 Q8_0 GEMM, timed with CUDA
+events at the batch's shape.  `cpu_baseline` times the CPU restatement of the
+same tower on this host's cores on a bounded sample (the reference's ggml CPU
+path cannot be built here: its ggml submodule is empty).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "hbd-siglip2.cpp_b200"))
+
+METRIC = "Q8_0 vision images/s at 1/2/4/8 B200; MMQ GEMM int8 TOPS vs peak"
+N_IMAGES = 512
+PATCH_DIM = 768
+# DRAM bytes per token of one fc1 launch (dram__bytes_read + dram__bytes_write)
+# from the ncu capture summarised in profiles/gemm_fc1_launch_traffic.md, scaled
+# to the batch's token count (traffic grows in proportion to M).
+FC1_DRAM_BYTES_PER_TOKEN = None
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get("bf16_tflops", 1590.0)), float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"b2q_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if not self.proc or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                if int(f[0]) not in self.gpus:
+                    continue
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons)}
+
+
+def shard(grids, rank, world):
+    """Length-balanced deal: sort images by patch count, deal round-robin."""
+    order = sorted(range(len(grids)), key=lambda i: -grids[i][0] * grids[i][1])
+    return sorted(order[rank::world])
+
+
+def cpu_tower_sample(threads=None):
+    """Time the CPU restatement of the tower on one 16x16-patch image (256
+    tokens), PROBE pooling, all host threads."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    from b2q import synth
+    O.build()
+    n = threads or os.cpu_count() or 1
+    O.set_threads(n)
+    ck = synth.vision_checkpoint(synth.TowerConfig(), seed=0)
+    x = synth.patches(256, PATCH_DIM, seed=1)
+    O.vision_encode(ck, x[:16], 4, 4, pooling=1)   # warm the library and threads
+    return O, ck, x, n
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    O, ck, x, cores = cpu_tower_sample()
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        O.vision_encode(ck, x, 16, 16, pooling=1)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+    total = sum(times)
+    value = args.steps / total
+    sample = "1 image of 16x16 = 256 patches per step (of the 512-image config-4 batch), PROBE pooling"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> fp32",
+        "data": "synthetic", "config": {"workload": "config-4 NaFlex vision tower (CPU sample)",
+                                        "model": "SigLIP2-so400m-patch16 vision, Q8_0", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--images", type=int, default=N_IMAGES)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    import b2q
+    from b2q import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    b2q.init(local)
+
+    cfg = synth.TowerConfig()
+    t0 = time.time()
+    ck = synth.vision_checkpoint(cfg, seed=0)
+    tower = b2q.VisionTower(cfg)
+    tower.load(ck)
+    log(f"[rank {rank}] weights ready in {time.time() - t0:.1f}s")
+
+    grids = synth.naflex_grids(args.images, seed=0)
+    mine = shard(grids, rank, world)
+    my_grids = [grids[i] for i in mine]
+    my_tokens = sum(h * w for h, w in my_grids)
+    total_tokens = sum(h * w for h, w in grids)
+    host = torch.empty((my_tokens, PATCH_DIM), dtype=torch.float32, pin_memory=True)
+    off = 0
+    for i in mine:
+        n = grids[i][0] * grids[i][1]
+        host[off:off + n] = torch.from_numpy(synth.patches(n, PATCH_DIM, seed=i))
+        off += n
+    dev = host.cuda()
+    tower.reserve(my_tokens, len(my_grids))
+    per_rank = (args.images + world - 1) // world
+    emb = torch.zeros((per_rank, cfg.hidden), dtype=torch.float32, device="cuda")
+    gathered = torch.zeros((world * per_rank, cfg.hidden), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def gather():
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, emb)
+        else:
+            gathered[:per_rank].copy_(emb)
+
+    def step_device():
+        tower.encode(dev, my_grids, b2q.POOL_PROBE, out=emb)
+        gather()
+
+    out_host = np.empty((len(my_grids), cfg.hidden), np.float32)
+    gathered_host = torch.empty((world * per_rank, cfg.hidden), dtype=torch.float32, pin_memory=True)
+
+    def step_e2e():
+        # public host-buffer entry point: pinned patches in, embeddings out
+        import ctypes as C
+        g = np.asarray(my_grids, np.int32).reshape(-1)
+        b2q.check(b2q.lib().b2q_vision_encode_host(tower.handle, host.data_ptr(), g.ctypes.data_as(b2q.I32P),
+                                                   len(my_grids), b2q.POOL_PROBE, out_host.ctypes.data,
+                                                   C.c_void_p(stream.cuda_stream)))
+        if world > 1:
+            emb[:len(my_grids)].copy_(torch.from_numpy(out_host), non_blocking=False)
+            dist.all_gather_into_tensor(gathered, emb)
+            if rank == 0:
+                gathered_host.copy_(gathered)
+
+    def timed(fn, steps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize()
+    b2q.check_device()
+
+    n0 = b2q.launch_count()
+    gpus_used = list(range(args.gpus)) if rank == 0 else []
+    with ClockSampler(gpus_used) as clk:
+        ms = timed(step_device, args.steps)
+    launches = b2q.launch_count() - n0
+    clocks = clk.summary()
+    b2q.check_device()
+
+    # end to end through the host-buffer entry point
+    step_e2e()
+    ms_e2e = timed(step_e2e, args.steps)
+
+    # roofline of the dominant kernel: fc1 GEMM (N=4304, K=1152) with the
+    # GELU->q8_1 epilogue at this rank's token count, CUDA events on the stream
+    W = b2q.Weight(ck.tensors["v.blk.0.ffn_up.weight"], cfg.ffn, cfg.hidden)
+    M = my_tokens
+    act = b2q.act_empty(M, cfg.hidden)
+    act_o = b2q.act_empty(M, cfg.ffn)
+    b2q.quantize_q8_1(torch.randn((M, cfg.hidden), device="cuda"), act, M, cfg.hidden)
+    bias = torch.zeros(cfg.ffn, device="cuda")
+    for _ in range(3):
+        b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
+    torch.cuda.synchronize()
+    reps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = e0.elapsed_time(e1) / reps
+    gemm_tops = 2.0 * M * cfg.ffn * cfg.hidden / (gemm_ms * 1e-3) / 1e12
+    W.release()
+
+    if rank == 0:
+        bf16_peak, hbm_peak, peak_src = peaks()
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            O, ck_cpu, x, cores = cpu_tower_sample()
+            t = time.perf_counter()
+            O.vision_encode(ck_cpu, x, 16, 16, pooling=1)
+            dt = time.perf_counter() - t
+            cpu = {"value": 1.0 / dt, "unit": "images/s", "cores": cores, "kind": "port",
+                   "sample": "1 image of 16x16 = 256 patches, PROBE pooling, CPU restatement (oracle/), "
+                             "OpenMP over all host threads"}
+        images = args.images * args.steps
+        traffic = (FC1_DRAM_BYTES_PER_TOKEN * M) if FC1_DRAM_BYTES_PER_TOKEN else None
+        line = {
+            "metric": METRIC, "value": images / (ms * 1e-3), "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> fp32 (Q8_0 x q8_1)",
+            "data": "synthetic",
+            "config": {"workload": "config-4: 512 NaFlex images (256-1024 patches, random grids), PROBE pooling",
+                       "model": "SigLIP2-so400m-patch16 vision tower, Q8_0 (27 layers, width 1152)",
+                       "global_batch": args.images, "tokens_per_step": total_tokens,
+                       "parallelism": f"image-sharded replicas x{world} + NCCL all-gather",
+                       "l2": "inputs and activations larger than L2 (no flush)"},
+            "e2e": {"value": images / (ms_e2e * 1e-3), "unit": "images/s",
+                    "h2d_bytes_per_step": int(total_tokens * PATCH_DIM * 4),
+                    "d2h_bytes_per_step": int(args.images * cfg.hidden * 4)},
+            "roofline": {"kernel": "gemm_q8_kernel (fc1, N=4304, K=1152, GELU->q8_1 epilogue)",
+                         "bound": "tensor", "achieved": gemm_tops, "peak": bf16_peak / 1.0, "unit": "TFLOP/s",
+                         "frac": gemm_tops / bf16_peak, "peak_source": f"bf16 dense, {peak_src}",
+                         "launch_ms": gemm_ms, "M": M, "traffic": traffic},
+            "gemm_tops": gemm_tops,
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -21,10 +21,13 @@ EPI_NONE, EPI_BIAS, EPI_BIAS_RESIDUAL, EPI_BIAS_GELU_Q8, EPI_BIAS_F16 = 0, 1, 2,
 
 #: every symbol include/b2q.h declares (checked by the CPU test suite)
 EXPORTS = [
-    "b2q_last_error", "b2q_abi_version", "b2q_init", "b2q_tune", "b2q_check_device",
+    "b2q_last_error", "b2q_abi_version", "b2q_launch_count", "b2q_init", "b2q_tune", "b2q_check_device",
     "b2q_weight_register", "b2q_weight_release", "b2q_weight_shape",
     "b2q_act_bytes", "b2q_act_layout", "b2q_quantize_q8_1", "b2q_ln_quantize_q8_1",
     "b2q_mul_mat_q8_0", "b2q_mul_mat_q8_0_f32", "b2q_block_sums",
+    "b2q_attention_scratch_bytes", "b2q_attention",
+    "b2q_vision_create", "b2q_vision_destroy", "b2q_vision_set_tensor", "b2q_vision_reserve",
+    "b2q_vision_encode", "b2q_vision_encode_host",
 ]
 
 
@@ -34,6 +37,15 @@ class B2QError(RuntimeError):
         self.status = status
 
 
+class VisionConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("ffn", C.c_int32), ("n_head", C.c_int32), ("n_layer", C.c_int32),
+                ("patch_dim", C.c_int32), ("pos_side", C.c_int32), ("eps", C.c_float)]
+
+
+POOL_MEAN, POOL_PROBE = 0, 1
+GGML_F32, GGML_Q8_0 = 0, 8
+
+
 class Epilogue(C.Structure):
     _fields_ = [("kind", C.c_int), ("bias", C.c_void_p), ("residual", C.c_void_p),
                 ("act_out", C.c_void_p), ("ld_out", C.c_int64)]
@@ -41,6 +53,7 @@ class Epilogue(C.Structure):
 
 _lib = None
 P, I64 = C.c_void_p, C.c_int64
+I32P = C.POINTER(C.c_int32)
 
 
 def lib():
@@ -51,6 +64,7 @@ def lib():
         L = C.CDLL(str(LIB_PATH))
         L.b2q_last_error.restype = C.c_char_p
         L.b2q_abi_version.restype = C.c_int
+        L.b2q_launch_count.restype = C.c_uint64
         L.b2q_init.argtypes = [C.c_int, C.c_int]
         L.b2q_check_device.argtypes = [P, C.POINTER(C.c_uint32)]
         L.b2q_tune.argtypes = [C.c_int, I64]
@@ -65,12 +79,27 @@ def lib():
         L.b2q_mul_mat_q8_0.argtypes = [P, P, I64, P, C.POINTER(Epilogue), P]
         L.b2q_mul_mat_q8_0_f32.argtypes = [P, P, I64, I64, P, P, P]
         L.b2q_block_sums.argtypes = [P, P, I64, P, P]
+        L.b2q_attention_scratch_bytes.argtypes = [I32P, C.c_int32]
+        L.b2q_attention_scratch_bytes.restype = C.c_size_t
+        L.b2q_attention.argtypes = [P, I64, P, I64, P, I64, I32P, I32P, I32P, I32P, I32P, C.c_int32, C.c_int32,
+                                    C.c_int32, P, I64, P, P]
+        L.b2q_vision_create.argtypes = [C.POINTER(VisionConfig), C.POINTER(P)]
+        L.b2q_vision_destroy.argtypes = [P]
+        L.b2q_vision_set_tensor.argtypes = [P, C.c_char_p, C.c_int32, P, I64, I64, P]
+        L.b2q_vision_reserve.argtypes = [P, I64, C.c_int32]
+        L.b2q_vision_encode.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
+        L.b2q_vision_encode_host.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
         for name in EXPORTS:
             fn = getattr(L, name)
-            if name not in ("b2q_last_error", "b2q_abi_version", "b2q_act_bytes"):
+            if name not in ("b2q_last_error", "b2q_abi_version", "b2q_act_bytes", "b2q_attention_scratch_bytes",
+                            "b2q_launch_count"):
                 fn.restype = C.c_int
         _lib = L
     return _lib
+
+
+def launch_count() -> int:
+    return int(lib().b2q_launch_count())
 
 
 def check(status: int):
@@ -94,7 +123,7 @@ def init(device: int = 0, ops_mode: int = -1):
     check(lib().b2q_init(device, ops_mode))
 
 
-TUNE_GEMM_BN, TUNE_TIMEOUT_NS = 1, 2
+TUNE_GEMM_BN, TUNE_TIMEOUT_NS, TUNE_ATTN_EXACT = 1, 2, 3
 
 
 def tune(key: int, value: int):
@@ -184,3 +213,86 @@ def mul_mat_f32(w: Weight, x, m: int, x_cols: int, y, scratch, stream=None):
 
 def block_sums(w: Weight, act, m: int, out, stream=None):
     check(lib().b2q_block_sums(w.handle, _ptr(act), m, _ptr(out), _stream(stream)))
+
+
+def _i32(a):
+    arr = np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+    return arr, arr.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+def attention(q, ldq, k, ldk, v, ldv, q_off, q_len, k_off, k_len, o_off, n_head, out, ldo, stream=None):
+    """Packed-sequence attention (head_dim 72); q/k/v fp16 torch tensors, out fp32."""
+    import torch
+    keep = [_i32(x) for x in (q_off, q_len, k_off, k_len, o_off)]
+    n_seq = len(keep[0][0])
+    nbytes = int(lib().b2q_attention_scratch_bytes(keep[1][1], n_seq))
+    scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device="cuda")
+    check(lib().b2q_attention(_ptr(q), ldq, _ptr(k), ldk, _ptr(v), ldv, keep[0][1], keep[1][1], keep[2][1],
+                              keep[3][1], keep[4][1], n_seq, n_head, 72, _ptr(out), ldo, _ptr(scratch),
+                              _stream(stream)))
+    return scratch
+
+
+class VisionTower:
+    """Batched SigLIP2 vision tower (the C++ driver behind b2q_vision_*)."""
+
+    def __init__(self, cfg):
+        self.cfg = cfg
+        c = VisionConfig(cfg.hidden, cfg.ffn, cfg.n_head, cfg.n_layer, cfg.patch_dim, cfg.pos_side, cfg.eps)
+        h = C.c_void_p()
+        check(lib().b2q_vision_create(C.byref(c), C.byref(h)))
+        self.handle = h
+
+    def set_tensor(self, name: str, arr: np.ndarray, q8_shape=None, stream=None):
+        arr = np.ascontiguousarray(arr)
+        if q8_shape is not None:
+            n, _, kp = q8_shape
+            check(lib().b2q_vision_set_tensor(self.handle, name.encode(), GGML_Q8_0, arr.ctypes.data, kp, n,
+                                              _stream(stream)))
+        else:
+            a = np.ascontiguousarray(arr, np.float32)
+            ne0 = a.shape[-1]
+            ne1 = a.size // ne0
+            check(lib().b2q_vision_set_tensor(self.handle, name.encode(), GGML_F32, a.ctypes.data, ne0, ne1,
+                                              _stream(stream)))
+
+    def load(self, ck, stream=None):
+        for name, arr in ck.tensors.items():
+            if not name.startswith("v."):
+                continue
+            self.set_tensor(name, arr, ck.q8_shapes.get(name), stream)
+
+    def reserve(self, max_tokens: int, max_images: int):
+        check(lib().b2q_vision_reserve(self.handle, max_tokens, max_images))
+
+    def encode(self, patches, grids, pooling=POOL_PROBE, out=None, stream=None):
+        """patches: torch CUDA fp32 [T][patch_dim] (images back to back); grids: [(h, w), ...]."""
+        import torch
+        g, gp = _i32(np.asarray(grids, np.int32).reshape(-1))
+        n = len(grids)
+        if out is None:
+            out = torch.empty((n, self.cfg.hidden), dtype=torch.float32, device="cuda")
+        check(lib().b2q_vision_encode(self.handle, _ptr(patches), gp, n, pooling, _ptr(out), _stream(stream)))
+        return out
+
+    def encode_host(self, patches: np.ndarray, grids, pooling=POOL_PROBE, out: np.ndarray | None = None,
+                    stream=None):
+        """Host in, host out (patch upload and embedding download included)."""
+        g, gp = _i32(np.asarray(grids, np.int32).reshape(-1))
+        n = len(grids)
+        if out is None:
+            out = np.empty((n, self.cfg.hidden), np.float32)
+        check(lib().b2q_vision_encode_host(self.handle, patches.ctypes.data, gp, n, pooling, out.ctypes.data,
+                                           _stream(stream)))
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().b2q_vision_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

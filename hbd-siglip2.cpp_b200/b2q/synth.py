@@ -186,15 +186,18 @@ def patches(n_tokens: int, patch_dim: int = 768, seed: int = 0) -> np.ndarray:
 
 
 def naflex_grids(n_images: int, lo: int = 256, hi: int = 1024, seed: int = 0):
-    """Per-image (h, w) grids with h*w uniform in [lo, hi]:
-    draw a patch count, then a random factor pair of it."""
+    """Per-image (h, w) patch grids for BASELINE config 4: a patch budget drawn
+    uniformly from [lo, hi] and an aspect ratio log-uniform in [1/4, 4] (the
+    range NaFlex resizing produces for ordinary photos), h = round(sqrt(n r)),
+    w = floor(n / h), so h * w stays inside [lo - h, hi]."""
     rng = np.random.default_rng(0xC4 ^ seed)
     grids = []
     for _ in range(n_images):
         n = int(rng.integers(lo, hi + 1))
-        divs = [d for d in range(1, n + 1) if n % d == 0]
-        h = int(divs[int(rng.integers(0, len(divs)))])
-        grids.append((h, n // h))
+        r = float(np.exp(rng.uniform(np.log(0.25), np.log(4.0))))
+        h = max(1, min(n, int(round(np.sqrt(n * r)))))
+        w = max(1, n // h)
+        grids.append((h, w))
     return grids
 
 

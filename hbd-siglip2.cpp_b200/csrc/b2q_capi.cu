@@ -3,6 +3,7 @@
 #include "b2q_internal.h"
 
 #include <cudaTypedefs.h>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -17,7 +18,10 @@ thread_local std::string t_last_error;
 DeviceState g_states[64];
 std::mutex g_init_mutex;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::atomic<uint64_t> g_launches{0};
 }  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 b2q_status set_error(b2q_status st, const std::string& msg) {
     t_last_error = msg;
@@ -55,15 +59,14 @@ static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 
 using namespace b2q;
 
-#define B2Q_REQUIRE_STATE()                                                                 \
-    DeviceState* ds = state();                                                              \
-    if (!ds) return set_error(B2Q_ERR_NOT_INIT, "b2q_init was not called for this device")
 
 extern "C" {
 
 const char* b2q_last_error(void) { return t_last_error.c_str(); }
 
 int b2q_abi_version(void) { return 1; }
+
+uint64_t b2q_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 b2q_status b2q_init(int device, int ops_mode) {
     if (device < 0 || device >= 64) return set_error(B2Q_ERR_INVALID, "device index out of range");
@@ -110,6 +113,9 @@ b2q_status b2q_tune(int key, int64_t value) {
         case B2Q_TUNE_TIMEOUT_NS:
             if (value < 1000000 || value > 60000000000ll) return set_error(B2Q_ERR_INVALID, "timeout must be in [1 ms, 60 s]");
             ds->timeout_ns = static_cast<uint64_t>(value);
+            return B2Q_OK;
+        case B2Q_TUNE_ATTN_EXACT:
+            ds->attn_exact = value ? 1 : 0;
             return B2Q_OK;
         default:
             return set_error(B2Q_ERR_INVALID, "unknown tuning key");
@@ -318,6 +324,44 @@ b2q_status b2q_block_sums(const b2q_weight* w, const void* act, int64_t M, int32
     a.epi = B2Q_EPI_NONE;
     a.dump = sums;
     return launch_gemm(a, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------- attention
+size_t b2q_attention_scratch_bytes(const int32_t* q_len, int32_t n_seq) {
+    if (!q_len || n_seq <= 0) return 0;
+    int64_t tiles = 0;
+    for (int32_t s = 0; s < n_seq; ++s) tiles += (q_len[s] + 63) / 64;
+    return attn_tiles_bytes(static_cast<int>(tiles));
+}
+
+b2q_status b2q_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                         const int32_t* q_off, const int32_t* q_len, const int32_t* k_off, const int32_t* k_len,
+                         const int32_t* o_off, int32_t n_seq, int32_t n_head, int32_t d_head, float* out, int64_t ldo,
+                         void* tiles_scratch, void* stream) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!q || !k || !v || !out || !q_off || !q_len || !k_off || !k_len || !o_off || !tiles_scratch)
+        return set_error(B2Q_ERR_INVALID, "null pointer");
+    if (d_head != 72) return set_error(B2Q_ERR_SHAPE, "only head_dim 72 is implemented");
+    if (n_seq <= 0 || n_head <= 0 || n_head > 65535) return set_error(B2Q_ERR_SHAPE, "bad n_seq / n_head");
+    if (ldq % 8 || ldk % 8 || ldv % 8 || ldo % 2 || !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) ||
+        !aligned(out, 8))
+        return set_error(B2Q_ERR_ALIGN, "attention rows need 16-byte aligned fp16 rows and 8-byte aligned output");
+    for (int32_t s = 0; s < n_seq; ++s)
+        if (q_len[s] < 0 || k_len[s] <= 0 || q_off[s] < 0 || k_off[s] < 0 || o_off[s] < 0)
+            return set_error(B2Q_ERR_SHAPE, "every sequence needs at least one key");
+    const size_t bytes = b2q_attention_scratch_bytes(q_len, n_seq);
+    std::string host(bytes, '\0');
+    const int n = attn_build_tiles(q_off, q_len, k_off, k_len, o_off, n_seq, host.data(),
+                                   static_cast<int>(bytes / attn_tiles_bytes(1)));
+    if (n < 0) return set_error(B2Q_ERR_SHAPE, "tile table overflow");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    b2q_status st = cuda_check(cudaMemcpyAsync(tiles_scratch, host.data(), bytes, cudaMemcpyHostToDevice, s),
+                               "attention tile upload");
+    if (st) return st;
+    return cuda_check(launch_attention(static_cast<const __half*>(q), ldq, static_cast<const __half*>(k), ldk,
+                                       static_cast<const __half*>(v), ldv, tiles_scratch, n, n_head, out, ldo, s),
+                      "attention launch");
 }
 
 }  // extern "C"

@@ -474,6 +474,7 @@ static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s) {
     const int tiles = p.m_tiles * p.n_tiles;
     const int grid = tiles < ds->num_sms ? tiles : ds->num_sms;
     gemm_q8_kernel<kOps, kBN, kDump><<<grid, Cfg::THREADS, Cfg::SMEM, s>>>(tmA, *tmB, tmDX, *tmDW, p);
+    count_launch();
     return cuda_check(cudaGetLastError(), "gemm launch");
 }
 

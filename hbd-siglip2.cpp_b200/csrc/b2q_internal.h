@@ -6,6 +6,7 @@
 #include <string>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 
 #include "../../include/b2q.h"
 
@@ -35,8 +36,10 @@ struct DeviceState {
     uint32_t* err = nullptr;      // device error word (cudaMalloc'ed at init)
     uint64_t timeout_ns = 2000000000ull;
     int gemm_bn = 0;              // GEMM tile width: 128, 256, or 0 = by shape
+    int attn_exact = 0;           // attention in the checker's fixed fp32 order
 };
 DeviceState* state();             // per-thread current device state
+void count_launch();              // every kernel launch of the library counts once
 b2q_status set_error(b2q_status st, const std::string& msg);
 b2q_status cuda_check(cudaError_t e, const char* what);
 
@@ -57,6 +60,10 @@ struct b2q_weight {
     CUtensorMap tm_d256, tm_d128;   // box {256,128} x (scales per stage)
 };
 
+#define B2Q_REQUIRE_STATE()                                                                 \
+    b2q::DeviceState* ds = b2q::state();                                                    \
+    if (!ds) return b2q::set_error(B2Q_ERR_NOT_INIT, "b2q_init was not called for this device")
+
 namespace b2q {
 // kernels (launchers return cudaError_t of the launch)
 cudaError_t launch_repack_q8_0(const void* raw, int64_t N, int64_t Kb, int64_t row_bytes, int mode, void* q,
@@ -65,6 +72,13 @@ cudaError_t launch_quantize_q8_1(const float* x, int64_t M, int64_t K, int64_t l
                                  cudaStream_t s);
 cudaError_t launch_ln_quant(const float* x, const float* w, const float* b, float eps, int64_t M, int64_t H,
                             void* act, float* y, int mode, cudaStream_t s);
+
+int attn_build_tiles(const int* q_off, const int* q_len, const int* k_off, const int* k_len, const int* o_off,
+                     int n_seq, void* tiles, int max_tiles);
+size_t attn_tiles_bytes(int n_tiles);
+cudaError_t launch_attention(const __half* q, int64_t ldq, const __half* k, int64_t ldk, const __half* v,
+                             int64_t ldv, const void* tiles_dev, int n_tiles, int n_head, float* out, int64_t ldo,
+                             cudaStream_t s);
 
 struct GemmArgs {
     const b2q_weight* w;

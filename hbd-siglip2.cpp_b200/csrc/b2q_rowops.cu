@@ -63,6 +63,7 @@ cudaError_t launch_repack_q8_0(const void* raw, int64_t N, int64_t Kb, int64_t r
         repack_q8_0_kernel<kOpsF16><<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(raw), N, Kb, row_bytes, q, d);
     else
         repack_q8_0_kernel<kOpsI8><<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(raw), N, Kb, row_bytes, q, d);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -152,6 +153,7 @@ cudaError_t launch_quantize_q8_1(const float* x, int64_t M, int64_t K, int64_t l
         quantize_q8_1_kernel<kOpsF16><<<grid, kRowWarps * 32, 0, s>>>(x, M, K, ldx, act, d, L.Kp, L.ld);
     else
         quantize_q8_1_kernel<kOpsI8><<<grid, kRowWarps * 32, 0, s>>>(x, M, K, ldx, act, d, L.Kp, L.ld);
+    count_launch();
     return cudaGetLastError();
 }
 
@@ -235,6 +237,7 @@ cudaError_t launch_ln_quant(const float* x, const float* w, const float* b, floa
             return cudaErrorInvalidValue;
     }
 #undef B2Q_LN_CASE
+    count_launch();
     return cudaGetLastError();
 }
 

@@ -48,15 +48,19 @@ enum {
 /* Thread-local description of the last failure on this thread. */
 const char *b2q_last_error(void);
 int b2q_abi_version(void);
+/* Kernel launches this library has issued in the process (all devices). */
+uint64_t b2q_launch_count(void);
 
 /* Per-device set-up (current device); allocates the device error word.
  * ops_mode: B2Q_OPS_I8 or B2Q_OPS_F16 (-1 = library default). */
 b2q_status b2q_init(int device, int ops_mode);
 /* Tuning knobs of the current device's state (reference precedent: the
  * SIGLIP2_* environment switches of src/cuda/siglip2_megakernel.cu:1378-1401).
- *   B2Q_TUNE_GEMM_BN:   GEMM tile width 128 or 256 (0 = chosen per shape)
- *   B2Q_TUNE_TIMEOUT_NS: bound of every in-kernel wait (default 2 s) */
-enum { B2Q_TUNE_GEMM_BN = 1, B2Q_TUNE_TIMEOUT_NS = 2 };
+ *   B2Q_TUNE_GEMM_BN:    GEMM tile width 128 or 256 (0 = default)
+ *   B2Q_TUNE_TIMEOUT_NS: bound of every in-kernel wait (default 2 s)
+ *   B2Q_TUNE_ATTN_EXACT: 1 = attention in one fixed fp32 order (slow; makes
+ *                        the tower bit-reproducible), 0 = tensor cores */
+enum { B2Q_TUNE_GEMM_BN = 1, B2Q_TUNE_TIMEOUT_NS = 2, B2Q_TUNE_ATTN_EXACT = 3 };
 b2q_status b2q_tune(int key, int64_t value);
 /* Reads (and clears) the device error word after synchronising `stream`. */
 b2q_status b2q_check_device(void *stream, uint32_t *code_out);
@@ -128,6 +132,58 @@ b2q_status b2q_mul_mat_q8_0_f32(const b2q_weight *w, const float *x, int64_t M, 
 
 /* Debug: the int32 block dots S[kb][m][n] (Kb*M*N int32) of one GEMM. */
 b2q_status b2q_block_sums(const b2q_weight *w, const void *act, int64_t M, int32_t *sums, void *stream);
+
+/* ---- attention (head_dim 72) ---------------------------------------------
+ * flash_attn_ext over packed sequences, replacing src/siglip2_vision.cpp:
+ * 154-175 with the QKV-prep / post-FA copies of src/cuda/siglip2_megakernel.cu:
+ * 166-267,358-394.  q, k, v: fp16 rows (row strides ldq/ldk/ldv elements),
+ * head h at column h*72.  Sequence s (host arrays, n_seq entries) has q_len[s]
+ * query rows from q_off[s], k_len[s] keys/values from k_off[s], and writes
+ * out[o_off[s] + i][h*72 + d] (fp32, row stride ldo).  Softmax scale
+ * 1/sqrt(72).  tiles_scratch: device memory of b2q_attention_scratch_bytes()
+ * for the same sequence description (the tile table is copied into it). */
+size_t b2q_attention_scratch_bytes(const int32_t *q_len, int32_t n_seq);
+b2q_status b2q_attention(const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v, int64_t ldv,
+                         const int32_t *q_off, const int32_t *q_len, const int32_t *k_off, const int32_t *k_len,
+                         const int32_t *o_off, int32_t n_seq, int32_t n_head, int32_t d_head, float *out, int64_t ldo,
+                         void *tiles_scratch, void *stream);
+
+/* ---- vision tower ----------------------------------------------------------
+ * Batched counterpart of siglip2::VisionEncoder (src/siglip2_vision.h:25-60;
+ * load src/siglip2_vision.cpp:424-599, encode :601-758).  Tensors are handed
+ * over by their GGUF names ("v.patch_embd.weight", "v.blk.N.attn_qkv.weight",
+ * "v.head.probe", ... as loaded at src/siglip2_vision.cpp:496-556) with the
+ * ggml type id (0 = F32, 8 = Q8_0) and ggml shape (ne0 innermost).  Q8_0 ffn_down
+ * tensors carry the zero K-padding 4304 -> 4320 (tools/siglip2-quantize/
+ * main.cpp:174-186).  A batch packs n_images images back to back: image i has
+ * grid_hw[2i] x grid_hw[2i+1] patches of patch_dim fp32 values (row-major
+ * over the grid); out receives n_images x hidden fp32 embeddings.  pooling
+ * follows siglip2::Pooling: MEAN = 0, PROBE = 1. */
+typedef struct b2q_vision b2q_vision;
+typedef struct b2q_vision_config {
+    int32_t hidden;     /* 1152 */
+    int32_t ffn;        /* 4304 */
+    int32_t n_head;     /* 16 (head_dim 72) */
+    int32_t n_layer;    /* 27 */
+    int32_t patch_dim;  /* 768 = 3 x 16 x 16 */
+    int32_t pos_side;   /* 16: the learned 16 x 16 position table */
+    float eps;          /* 1e-6 */
+} b2q_vision_config;
+enum { B2Q_POOL_MEAN = 0, B2Q_POOL_PROBE = 1 };
+b2q_status b2q_vision_create(const b2q_vision_config *cfg, b2q_vision **out);
+b2q_status b2q_vision_destroy(b2q_vision *v);
+b2q_status b2q_vision_set_tensor(b2q_vision *v, const char *name, int32_t ggml_type, const void *host_data,
+                                 int64_t ne0, int64_t ne1, void *stream);
+/* Workspace for batches of up to max_tokens patches / max_images images
+ * (allocates; encode calls with larger batches grow it). */
+b2q_status b2q_vision_reserve(b2q_vision *v, int64_t max_tokens, int32_t max_images);
+/* Device in, device out (patches [T][patch_dim], out [n_images][hidden]). */
+b2q_status b2q_vision_encode(b2q_vision *v, const float *patches, const int32_t *grid_hw, int32_t n_images,
+                             int32_t pooling, float *out, void *stream);
+/* Host in, host out: uploads the patches, encodes, downloads the embeddings
+ * and synchronises `stream`. */
+b2q_status b2q_vision_encode_host(b2q_vision *v, const float *patches_host, const int32_t *grid_hw,
+                                  int32_t n_images, int32_t pooling, float *out_host, void *stream);
 
 #ifdef __cplusplus
 }

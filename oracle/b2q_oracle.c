@@ -325,6 +325,50 @@ void orc_layernorm(const float *x, const float *w, const float *b, float eps,
 /* Attention — flash_attn_ext with K/V cast to fp16 and F32 precision        */
 /* (siglip2_vision.cpp:154-175), kq_scale = 1/sqrt(d_head) (:629-632).       */
 /* ------------------------------------------------------------------------ */
+/* Attention of the quantized (Q8) towers: one fixed fp32 evaluation order,
+ * reproduced operation by operation by the GPU's exact attention mode.  Q, K
+ * and V arrive as fp16 values (the QKV projection's output rounded to fp16;
+ * K and V are cast to fp16 by the reference graph, siglip2_vision.cpp:
+ * 164-165); with GGML_PREC_F32 (siglip2_vision.cpp:167) scores, softmax and
+ * the weighted sum are fp32:
+ *   s_k = fma-chain over d ascending of q_d*k_kd, times 1/sqrt(d_head)
+ *   m = max_k s_k ; p_k = exp(s_k - m) (the library's own exp) ;
+ *   l = sum_k p_k (keys ascending) ; o_d = fma-chain over k of p_k*v_kd, / l
+ * q/k/v point at head 0 of row 0 with row strides ldq/ldk/ldv; Lq query rows
+ * attend to Lk keys; out rows stride ldo. */
+static void attention_q8(const float *q, int64_t ldq, const float *k, int64_t ldk, const float *v, int64_t ldv,
+                         int64_t Lq, int64_t Lk, int64_t n_head, int64_t dh, float *out, int64_t ldo) {
+    const float scale = 1.0f / sqrtf((float) dh);
+    #pragma omp parallel for schedule(static) collapse(2)
+    for (int64_t hd = 0; hd < n_head; ++hd) {
+        for (int64_t qi = 0; qi < Lq; ++qi) {
+            const float *qr = q + qi * ldq + hd * dh;
+            float *s = (float *) malloc((size_t) Lk * sizeof(float));
+            float m = -INFINITY;
+            for (int64_t kk = 0; kk < Lk; ++kk) {
+                const float *kr = k + kk * ldk + hd * dh;
+                float dot = 0.0f;
+                for (int64_t d = 0; d < dh; ++d) dot = fmaf(qr[d], kr[d], dot);
+                s[kk] = dot * scale;
+                m = fmaxf(m, s[kk]);
+            }
+            float l = 0.0f;
+            for (int64_t kk = 0; kk < Lk; ++kk) {
+                s[kk] = orc_expf(s[kk] - m);
+                l = l + s[kk];
+            }
+            for (int64_t d = 0; d < dh; ++d) {
+                float acc = 0.0f;
+                for (int64_t kk = 0; kk < Lk; ++kk) acc = fmaf(s[kk], v[kk * ldv + hd * dh + d], acc);
+                out[qi * ldo + hd * dh + d] = acc / l;
+            }
+            free(s);
+        }
+    }
+}
+
+static inline float half_of(float v) { return orc_fp16_to_fp32(orc_fp32_to_fp16(v)); }
+
 void orc_attention(const float *qkv, int64_t T, int64_t H, int64_t n_head,
                    const int64_t *seq_off, const int64_t *seq_len, int64_t n_seq,
                    float *out) {
@@ -474,7 +518,16 @@ static void encoder_block(const orc_block *B, float *x, int64_t T, int64_t H, in
     orc_layernorm(x, B->ln1_w, B->ln1_b, eps, T, H, ln);
     proj(B->qkv_w, 3 * H, H, H, ln, T, quant_act, qkv);
     add_bias(qkv, B->qkv_b, T, 3 * H);
-    orc_attention(qkv, T, H, n_head, seq_off, seq_len, n_seq, att);
+    if (quant_act) {
+        for (int64_t i = 0; i < T * 3 * H; ++i) qkv[i] = half_of(qkv[i]);
+        for (int64_t sidx = 0; sidx < n_seq; ++sidx) {
+            const float *base = qkv + seq_off[sidx] * 3 * H;
+            attention_q8(base, 3 * H, base + H, 3 * H, base + 2 * H, 3 * H, seq_len[sidx], seq_len[sidx], n_head,
+                         H / n_head, att + seq_off[sidx] * H, H);
+        }
+    } else {
+        orc_attention(qkv, T, H, n_head, seq_off, seq_len, n_seq, att);
+    }
     proj(B->o_w, H, H, H, att, T, quant_act, o);
     for (int64_t t = 0; t < T; ++t)
         for (int64_t i = 0; i < H; ++i)
@@ -496,6 +549,7 @@ static void encoder_block(const orc_block *B, float *x, int64_t T, int64_t H, in
 int orc_vision_encode(const orc_vision_weights *W, const float *patches,
                       int64_t h, int64_t w, int pooling, int quant_act, float *out) {
     const int64_t H = W->H, T = h * w;
+
     float *x   = (float *) malloc((size_t) T * H * sizeof(float));
     float *pos = (float *) malloc((size_t) T * H * sizeof(float));
 
@@ -546,8 +600,12 @@ int orc_vision_encode(const orc_vision_weights *W, const float *patches,
             memcpy(qkv + (t + 1) * 3 * H + H, k + t * H, (size_t) H * sizeof(float));
             memcpy(qkv + (t + 1) * 3 * H + 2 * H, v + t * H, (size_t) H * sizeof(float));
         }
-        /* single query against T keys: attention over rows 1..T with query row 0 */
-        {
+        /* single query against T keys */
+        if (quant_act) {
+            for (int64_t i = 0; i < H; ++i) q[i] = half_of(q[i]);
+            for (int64_t i = 0; i < T * H; ++i) { k[i] = half_of(k[i]); v[i] = half_of(v[i]); }
+            attention_q8(q, 0, k, H, v, H, 1, T, W->n_head, H / W->n_head, att, H);
+        } else {
             const int64_t dh = H / W->n_head;
             const float scale = 1.0f / sqrtf((float) dh);
             for (int64_t hd = 0; hd < W->n_head; ++hd) {
@@ -555,10 +613,8 @@ int orc_vision_encode(const orc_vision_weights *W, const float *patches,
                 double mx = -INFINITY;
                 for (int64_t t = 0; t < T; ++t) {
                     double dot = 0.0;
-                    for (int64_t i = 0; i < dh; ++i) {
-                        float kv = orc_fp16_to_fp32(orc_fp32_to_fp16(k[t * H + hd * dh + i]));
-                        dot += (double) q[hd * dh + i] * (double) kv;
-                    }
+                    for (int64_t i = 0; i < dh; ++i)
+                        dot += (double) q[hd * dh + i] * (double) half_of(k[t * H + hd * dh + i]);
                     sc[t] = dot * (double) scale;
                     if (sc[t] > mx) mx = sc[t];
                 }
@@ -566,8 +622,7 @@ int orc_vision_encode(const orc_vision_weights *W, const float *patches,
                 for (int64_t t = 0; t < T; ++t) { sc[t] = exp(sc[t] - mx); den += sc[t]; }
                 for (int64_t i = 0; i < dh; ++i) {
                     double acc = 0.0;
-                    for (int64_t t = 0; t < T; ++t)
-                        acc += sc[t] * (double) orc_fp16_to_fp32(orc_fp32_to_fp16(v[t * H + hd * dh + i]));
+                    for (int64_t t = 0; t < T; ++t) acc += sc[t] * (double) half_of(v[t * H + hd * dh + i]);
                     att[hd * dh + i] = (float) (acc / den);
                 }
                 free(sc);
@@ -590,6 +645,7 @@ int orc_vision_encode(const orc_vision_weights *W, const float *patches,
 int orc_text_encode(const orc_text_weights *W, const int32_t *ids, int64_t n_prompts,
                     int quant_act, float *out) {
     const int64_t H = W->H, P = W->n_pos, T = n_prompts * P;
+
     const int64_t Kb = H / 32;
     float *x = (float *) malloc((size_t) T * H * sizeof(float));
     /* get_rows(token_embd Q8_0) dequantizes the row; + position row (siglip2_text.cpp:837-847) */

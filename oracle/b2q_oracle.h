@@ -72,7 +72,9 @@ void orc_layernorm(const float *x, const float *w, const float *b, float eps,
 /* ---- attention ---------------------------------------------------------- */
 /* qkv: [T][3H] fp32 rows laid out [Q | K | V], head h at offset h*dh inside
  * each (siglip2_vision.cpp:198-206).  K and V are rounded to fp16 before use
- * (siglip2_vision.cpp:164-165); scores/softmax/accumulation in fp32.
+ * (siglip2_vision.cpp:164-165); scores, softmax and accumulation in double.
+ * (The quantized towers use the fixed fp32 order documented at attention_q8
+ * in b2q_oracle.c instead.)
  * key_len (may be NULL) limits the keys of each sequence; seq_off/seq_len
  * describe n_seq packed sequences.  out: [T][H]. */
 void orc_attention(const float *qkv, int64_t T, int64_t H, int64_t n_head,

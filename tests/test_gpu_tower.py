@@ -1,0 +1,128 @@
+"""GPU vision tower (C++ driver over the Q8_0 kernels) against the CPU oracle's
+tower restatement on the same seeded synthetic checkpoint.
+
+Two bars:
+* exact attention mode (B2Q_TUNE_ATTN_EXACT): the whole tower, 27 layers and
+  both poolings, is bit-identical to the oracle — every kernel follows the
+  oracle's fixed fp32 operation order;
+* default tensor-core attention (fp16 Q and P, fp32 accumulation, as ggml's
+  flash attention): cosine >= 0.9999.  Any attention
+  that is not bit-reproducible moves some q8_1 rounding decisions downstream;
+  over 27 layers that moves pooled values by up to ~0.03 (measured on the CPU
+  between two oracle attention precisions: 0.023-0.028 on values of ~2), so
+  the max-abs bar here is 0.05 rather than the north star's 2e-3, which only
+  a bit-reproducible attention can meet (the exact mode does, with 0).
+"""
+import numpy as np
+import pytest
+
+import b2q
+from b2q import synth
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    b2q.init(0)
+
+
+def cos(a, b):
+    return float(np.dot(a, b) / np.linalg.norm(a) / np.linalg.norm(b))
+
+
+def run_tower(ck, grids, pooling, seed=0):
+    cfg = ck.cfg
+    tower = b2q.VisionTower(cfg)
+    tower.load(ck)
+    patches = [synth.patches(h * w, cfg.patch_dim, seed=seed + i) for i, (h, w) in enumerate(grids)]
+    packed = torch.from_numpy(np.concatenate(patches)).cuda()
+    out = tower.encode(packed, grids, pooling)
+    torch.cuda.synchronize()
+    assert b2q.check_device() == 0
+    return tower, patches, out.cpu().numpy()
+
+
+def assert_matches(oracle, ck, patches, grids, got, pooling, exact=False):
+    for i, ((h, w), x) in enumerate(zip(grids, patches)):
+        ref = oracle.vision_encode(ck, x, h, w, pooling=pooling, quant_act=True)
+        if exact:
+            np.testing.assert_array_equal(got[i], ref, err_msg=f"image {i} grid {(h, w)}")
+            continue
+        c, e = cos(got[i], ref), float(np.abs(got[i] - ref).max())
+        assert c >= 0.9999 and e <= 0.05, (i, (h, w), c, e)
+
+
+@pytest.fixture
+def exact_attention(dev):
+    b2q.tune(b2q.TUNE_ATTN_EXACT, 1)
+    yield
+    b2q.tune(b2q.TUNE_ATTN_EXACT, 0)
+
+
+@pytest.mark.parametrize("pooling", [b2q.POOL_PROBE, b2q.POOL_MEAN])
+def test_tower_bit_exact_small_batch(oracle, exact_attention, pooling):
+    cfg = synth.TowerConfig(n_layer=3)
+    ck = synth.vision_checkpoint(cfg, seed=11, bias_std=0.02, ln_std=0.1)
+    grids = [(16, 16), (12, 20), (5, 9), (27, 27), (1, 3), (2, 40)]
+    _, patches, got = run_tower(ck, grids, pooling)
+    assert_matches(oracle, ck, patches, grids, got, pooling, exact=True)
+
+
+def test_tower_bit_exact_full_depth(oracle, exact_attention):
+    # all 27 layers at the reference's native 16x16 grid (config 1 geometry)
+    ck = synth.vision_checkpoint(synth.TowerConfig(), seed=0)
+    grids = [(16, 16)]
+    _, patches, got = run_tower(ck, grids, b2q.POOL_PROBE)
+    assert_matches(oracle, ck, patches, grids, got, b2q.POOL_PROBE, exact=True)
+
+
+@pytest.mark.parametrize("pooling", [b2q.POOL_PROBE, b2q.POOL_MEAN])
+def test_tower_small_batch_varlen(oracle, dev, pooling):
+    # tensor-core attention; degenerate few-patch images are covered by the
+    # bit-exact tests above
+    cfg = synth.TowerConfig(n_layer=3)
+    ck = synth.vision_checkpoint(cfg, seed=11, bias_std=0.02, ln_std=0.1)
+    grids = [(16, 16), (12, 20), (5, 9), (27, 27)]
+    _, patches, got = run_tower(ck, grids, pooling)
+    assert_matches(oracle, ck, patches, grids, got, pooling)
+
+
+def test_tower_full_depth_one_image(oracle, dev):
+    # all 27 layers, the reference's native 16x16 grid (config 1 geometry at 256 patches)
+    ck = synth.vision_checkpoint(synth.TowerConfig(), seed=0)
+    grids = [(16, 16)]
+    _, patches, got = run_tower(ck, grids, b2q.POOL_PROBE)
+    assert_matches(oracle, ck, patches, grids, got, b2q.POOL_PROBE)
+
+
+def test_tower_batching_is_exact(dev):
+    # an image's embedding must not depend on what else is in the batch
+    cfg = synth.TowerConfig(n_layer=2)
+    ck = synth.vision_checkpoint(cfg, seed=5, bias_std=0.02, ln_std=0.1)
+    grids = [(7, 11), (16, 16), (3, 30)]
+    tower, patches, batch = run_tower(ck, grids, b2q.POOL_PROBE)
+    for i, (h, w) in enumerate(grids):
+        single = tower.encode(torch.from_numpy(patches[i]).cuda(), [(h, w)], b2q.POOL_PROBE).cpu().numpy()
+        np.testing.assert_array_equal(single[0], batch[i])
+
+
+def test_tower_host_entry_point(dev):
+    cfg = synth.TowerConfig(n_layer=1)
+    ck = synth.vision_checkpoint(cfg, seed=2)
+    grids = [(4, 4), (2, 8)]
+    tower, patches, dev_out = run_tower(ck, grids, b2q.POOL_PROBE)
+    host_out = tower.encode_host(np.concatenate(patches), grids, b2q.POOL_PROBE)
+    np.testing.assert_array_equal(host_out, dev_out)
+
+
+def test_tower_missing_tensor_is_an_error(dev):
+    cfg = synth.TowerConfig(n_layer=1)
+    tower = b2q.VisionTower(cfg)
+    x = torch.zeros((4, cfg.patch_dim), device="cuda")
+    with pytest.raises(b2q.B2QError) as e:
+        tower.encode(x, [(2, 2)], b2q.POOL_MEAN)
+    assert e.value.status == b2q.ERR_INVALID
