@@ -24,7 +24,7 @@ EXPORTS = [
     "b2q_last_error", "b2q_abi_version", "b2q_launch_count", "b2q_init", "b2q_tune", "b2q_check_device",
     "b2q_weight_register", "b2q_weight_release", "b2q_weight_shape",
     "b2q_act_bytes", "b2q_act_layout", "b2q_quantize_q8_1", "b2q_ln_quantize_q8_1",
-    "b2q_mul_mat_q8_0", "b2q_mul_mat_q8_0_f32", "b2q_block_sums",
+    "b2q_mul_mat_q8_0", "b2q_mul_mat_q8_0_f32", "b2q_mul_mat_q8_0_f32_noalloc", "b2q_block_sums",
     "b2q_attention_scratch_bytes", "b2q_attention",
     "b2q_vision_create", "b2q_vision_destroy", "b2q_vision_set_tensor", "b2q_vision_reserve",
     "b2q_vision_encode", "b2q_vision_encode_host",
@@ -78,6 +78,7 @@ def lib():
         L.b2q_ln_quantize_q8_1.argtypes = [P, P, P, C.c_float, I64, I64, P, P, P]
         L.b2q_mul_mat_q8_0.argtypes = [P, P, I64, P, C.POINTER(Epilogue), P]
         L.b2q_mul_mat_q8_0_f32.argtypes = [P, P, I64, I64, P, P, P]
+        L.b2q_mul_mat_q8_0_f32_noalloc.argtypes = [P, P, I64, I64, P, P]
         L.b2q_block_sums.argtypes = [P, P, I64, P, P]
         L.b2q_attention_scratch_bytes.argtypes = [I32P, C.c_int32]
         L.b2q_attention_scratch_bytes.restype = C.c_size_t
@@ -209,6 +210,15 @@ def mul_mat(w: Weight, act, m: int, y=None, kind: int = EPI_NONE, bias=None, res
 
 def mul_mat_f32(w: Weight, x, m: int, x_cols: int, y, scratch, stream=None):
     check(lib().b2q_mul_mat_q8_0_f32(w.handle, _ptr(x), m, x_cols, _ptr(y), _ptr(scratch), _stream(stream)))
+
+
+def mul_mat_f32_noalloc(w: Weight, x, m: int, x_cols: int, y, stream=None):
+    """ggml_mul_mat without caller scratch: uses the library's fixed device
+    array (B2Q_NOALLOC_MAX_SCRATCH_BYTES), for callers that cannot allocate."""
+    check(lib().b2q_mul_mat_q8_0_f32_noalloc(w.handle, _ptr(x), m, x_cols, _ptr(y), _stream(stream)))
+
+
+NOALLOC_MAX_SCRATCH_BYTES = 32 << 20
 
 
 def block_sums(w: Weight, act, m: int, out, stream=None):

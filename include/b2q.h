@@ -130,6 +130,20 @@ b2q_status b2q_mul_mat_q8_0(const b2q_weight *w, const void *act, int64_t M, voi
 b2q_status b2q_mul_mat_q8_0_f32(const b2q_weight *w, const float *x, int64_t M, int64_t x_cols, float *y,
                                 void *act_scratch, void *stream);
 
+/* ggml_mul_mat like b2q_mul_mat_q8_0_f32, for callers that cannot allocate
+ * device memory (no counterpart in the reference): an op hook inside another
+ * framework's graph executor gets only the op's tensors and may not call
+ * cudaMalloc mid-graph.  The q8_1 scratch is a fixed array of
+ * B2Q_NOALLOC_MAX_SCRATCH_BYTES inside the library, reserved on every GPU
+ * that loads it until the process exits; calls needing more
+ * (b2q_act_bytes(M, K) > the maximum) fail with B2Q_ERR_SHAPE.  The first
+ * call on a device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race. */
+#define B2Q_NOALLOC_MAX_SCRATCH_BYTES (32u << 20)
+b2q_status b2q_mul_mat_q8_0_f32_noalloc(const b2q_weight *w, const float *x, int64_t M, int64_t x_cols, float *y,
+                                        void *stream);
+
 /* Debug: the int32 block dots S[kb][m][n] (Kb*M*N int32) of one GEMM. */
 b2q_status b2q_block_sums(const b2q_weight *w, const void *act, int64_t M, int32_t *sums, void *stream);
 
