@@ -14,14 +14,16 @@
 // integer below 2^24) into a ring of TMEM accumulators (512 columns / BN
 // deep), and the epilogue warps rescale-and-accumulate each block in
 // registers with packed f32x2 math while the tensor core runs ahead.  That
-// rescale (two fp32 operations per output element per K block) is the
-// kernel's bound, so the epilogue runs 16 warps — four per SM sub-partition —
-// to keep the FP32 pipes busy through TMEM-load and barrier latencies.
+// rescale (two fp32 operations per output element per K block) bounds the
+// kernel, so the epilogue loop carries almost nothing else: ring positions
+// advance without divisions, the K-block loop is unrolled per stage, and each
+// thread's 32-column TMEM load for the next chunk is in flight while it
+// computes the current one.
 //
-// Warp roles (640 threads, five warpgroups): warpgroup 0 holds the TMA
+// Warp roles (384 threads, three warpgroups): warpgroup 0 holds the TMA
 // producer (warp 0) and the TMEM owner / MMA issuer (warp 1) and gives most of
-// its registers to warpgroups 1-4, the sixteen epilogue warps (four per 32-lane
-// TMEM quadrant, each owning BN/4 output columns of its 32 rows).
+// its registers to warpgroups 1-2, the eight epilogue warps (two per 32-lane
+// TMEM quadrant, each owning BN/2 output columns of its 32 rows).
 #include "b2q_internal.h"
 #include "b2q_numerics.cuh"
 #include "b2q_ptx.cuh"
@@ -40,22 +42,21 @@ struct GemmCfg {
     static constexpr int DX_BYTES = KBS * BM * 4;
     static constexpr int DW_BYTES = KBS * BN * 4;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + DX_BYTES + DW_BYTES;
+    static constexpr int STAGES = 4;                       // power of two: ring position is a mask
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM_BUDGET = 227 * 1024 - BAR_BYTES - 1024;
-    static constexpr int STAGES = SMEM_BUDGET / STAGE_BYTES > 6 ? 6 : SMEM_BUDGET / STAGE_BYTES;
     static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-    static constexpr int EPI_WARPS = 16;
-    static constexpr int THREADS = 128 + EPI_WARPS * 32;   // 640: launch allocation 96 regs/thread
-    static constexpr int WG0_REGS = 40;                    // 128*40 + 512*104 <= 640*96
-    static constexpr int EPI_REGS = 104;
-    static constexpr int COLS = BN / 4;                    // columns per epilogue thread
+    static constexpr int EPI_WARPS = 8;
+    static constexpr int THREADS = 128 + EPI_WARPS * 32;   // 384: launch allocation 168 regs/thread
+    static constexpr int WG0_REGS = 56;                    // 128*56 + 256*224 = 384*168
+    static constexpr int EPI_REGS = 224;
+    static constexpr int COLS = BN / 2;                    // columns per epilogue thread
     static constexpr int CH = COLS / 32;                   // 32-column TMEM loads per K block
-    static constexpr int NBUF = 512 / BN;                  // accumulator ring depth
+    static constexpr int NBUF = 512 / BN;                  // accumulator ring depth (power of two)
     static constexpr int TMEM_COLS = 512;
     static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment for the swizzle");
-    static_assert(CH >= 1, "at least one 32-column chunk per thread");
-    static_assert(WG0_REGS * 128 + EPI_REGS * EPI_WARPS * 32 <= THREADS * 96, "register split exceeds the launch");
-    static_assert(STAGES >= 2, "pipeline needs two stages");
+    static_assert(CH % 2 == 0, "register double-buffer parity must repeat every K block");
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(WG0_REGS * 128 + EPI_REGS * EPI_WARPS * 32 <= THREADS * 168, "register split exceeds the launch");
 };
 
 struct GemmParams {
@@ -89,24 +90,308 @@ __device__ __forceinline__ float carrier_to_float(uint32_t r) {
     }
 }
 
-// acc[i] (i < 16) += ((float)S * dW) * dX for the 32 columns of one chunk;
-// r[i] holds the raw accumulator pair of columns 2i, 2i+1.
+// acc[i] (i < 16) += ((float)S * dW) * dX for the 32 columns of one chunk.
 template <int kOps>
-__device__ __forceinline__ float2 carrier_pair(uint64_t r) {
-    const uint32_t lo = static_cast<uint32_t>(r), hi = static_cast<uint32_t>(r >> 32);
-    return make_float2(carrier_to_float<kOps>(lo), carrier_to_float<kOps>(hi));
-}
-
-template <int kOps>
-__device__ __forceinline__ void rescale_chunk(float2* acc, const uint64_t (&r)[16], const float4* w4, float2 dx2) {
+__device__ __forceinline__ void rescale_chunk(float2* acc, const uint32_t (&r)[32], const float4* w4, float2 dx2) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float4 w = w4[i];
-        const float2 t01 = __fmul2_rn(carrier_pair<kOps>(r[2 * i]), make_float2(w.x, w.y));
-        const float2 t23 = __fmul2_rn(carrier_pair<kOps>(r[2 * i + 1]), make_float2(w.z, w.w));
+        const float2 f01 = make_float2(carrier_to_float<kOps>(r[4 * i + 0]), carrier_to_float<kOps>(r[4 * i + 1]));
+        const float2 f23 = make_float2(carrier_to_float<kOps>(r[4 * i + 2]), carrier_to_float<kOps>(r[4 * i + 3]));
+        const float2 t01 = __fmul2_rn(f01, make_float2(w.x, w.y));
+        const float2 t23 = __fmul2_rn(f23, make_float2(w.z, w.w));
         acc[2 * i] = __ffma2_rn(t01, dx2, acc[2 * i]);
         acc[2 * i + 1] = __ffma2_rn(t23, dx2, acc[2 * i + 1]);
     }
+}
+
+// Ring position: index and phase bit, advanced without divisions.
+template <int N>
+struct Ring {
+    uint32_t idx = 0, phase = 0;
+    __device__ __forceinline__ void next() {
+        if (++idx == N) {
+            idx = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
+struct Smem {
+    uint8_t* base;
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* tfull;
+    uint64_t* tempty;
+    volatile uint32_t* abort_flag;
+};
+
+// ---------------------------------------------------------------- producer
+template <int kOps, int kBN>
+__device__ bool run_producer(const Smem& sm, const CUtensorMap* tmA, const CUtensorMap* tmB, const CUtensorMap* tmDX,
+                             const CUtensorMap* tmDW, const GemmParams& p, uint32_t& issued) {
+    using Cfg = GemmCfg<kOps, kBN>;
+    const int num_tiles = p.m_tiles * p.n_tiles;
+    const int nst = (p.Kb + Cfg::KBS - 1) / Cfg::KBS;
+    Ring<Cfg::STAGES> st_ring;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles;
+        for (int st = 0; st < nst; ++st) {
+            const uint32_t s = st_ring.idx;
+            if (!mbar_wait(&sm.empty[s], st_ring.phase ^ 1u, sm.abort_flag, p.timeout_ns)) {
+                raise_error(p.err, sm.abort_flag, kDevTimeoutEmpty);
+                return false;
+            }
+            uint8_t* sbase = sm.base + s * Cfg::STAGE_BYTES;
+            mbar_arrive_expect_tx(&sm.full[s], Cfg::STAGE_BYTES);
+            const int kx = st * (Cfg::KROW / Cfg::ES);
+            tma_load_2d(sbase, tmA, &sm.full[s], kx, mb * Cfg::BM);
+            tma_load_2d(sbase + Cfg::A_BYTES, tmB, &sm.full[s], kx, nb * Cfg::BN);
+            tma_load_2d(sbase + Cfg::A_BYTES + Cfg::B_BYTES, tmDX, &sm.full[s], mb * Cfg::BM, st * Cfg::KBS);
+            tma_load_2d(sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES, tmDW, &sm.full[s], nb * Cfg::BN,
+                        st * Cfg::KBS);
+            ++issued;
+            st_ring.next();
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- MMA issuer
+template <int kOps, int kBN>
+__device__ bool run_mma(const Smem& sm, uint32_t tmem_base, const GemmParams& p, uint32_t& issued) {
+    using Cfg = GemmCfg<kOps, kBN>;
+    const uint32_t idesc = kOps == kOpsF16 ? idesc_f16_f32(Cfg::BM, Cfg::BN) : idesc_i8_s32(Cfg::BM, Cfg::BN);
+    const int num_tiles = p.m_tiles * p.n_tiles;
+    const int nst = (p.Kb + Cfg::KBS - 1) / Cfg::KBS;
+    Ring<Cfg::STAGES> st_ring;
+    Ring<Cfg::NBUF> acc_ring;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        for (int st = 0; st < nst; ++st) {
+            const uint32_t s = st_ring.idx;
+            if (!mbar_wait(&sm.full[s], st_ring.phase, sm.abort_flag, p.timeout_ns)) {
+                raise_error(p.err, sm.abort_flag, kDevTimeoutFull);
+                return false;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(sm.base + s * Cfg::STAGE_BYTES);
+            const uint32_t b_base = a_base + Cfg::A_BYTES;
+            const int nkb = min(Cfg::KBS, p.Kb - st * Cfg::KBS);
+            for (int j = 0; j < nkb; ++j) {
+                const uint32_t b = acc_ring.idx;
+                if (!mbar_wait(&sm.tempty[b], acc_ring.phase ^ 1u, sm.abort_flag, p.timeout_ns)) {
+                    raise_error(p.err, sm.abort_flag, kDevTimeoutTmemEmpty);
+                    return false;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + b * Cfg::BN;
+                if constexpr (kOps == kOpsF16) {
+                    mma_f16(d, smem_desc_k_sw128(a_base + j * 64), smem_desc_k_sw128(b_base + j * 64), idesc, 0u);
+                    mma_f16(d, smem_desc_k_sw128(a_base + j * 64 + 32), smem_desc_k_sw128(b_base + j * 64 + 32), idesc,
+                            1u);
+                } else {
+                    mma_i8(d, smem_desc_k_sw128(a_base + j * 32), smem_desc_k_sw128(b_base + j * 32), idesc, 0u);
+                }
+                mma_commit(&sm.tfull[b]);
+                ++issued;
+                acc_ring.next();
+            }
+            mma_commit(&sm.empty[s]);
+            st_ring.next();
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- epilogue
+template <int kOps, int kBN>
+__device__ __forceinline__ void store_tile(const GemmParams& p, float2 (&acc)[GemmCfg<kOps, kBN>::COLS / 2], int m,
+                                           int nbase) {
+    using Cfg = GemmCfg<kOps, kBN>;
+    if (m >= p.M) return;
+    if (p.epi == B2Q_EPI_BIAS_GELU_Q8) {
+        const int64_t kb_out0 = nbase / 32;
+#pragma unroll
+        for (int blk = 0; blk < Cfg::COLS / 32; ++blk) {
+            const int n0 = nbase + blk * 32;
+            if (n0 >= p.Kp_out) break;
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int n = n0 + 2 * i;
+                const float b0 = (p.bias && n < p.N) ? p.bias[n] : 0.0f;
+                const float b1 = (p.bias && n + 1 < p.N) ? p.bias[n + 1] : 0.0f;
+                float2& a2 = acc[blk * 16 + i];
+                a2.x = gelu_tanh(__fadd_rn(a2.x, b0));
+                a2.y = gelu_tanh(__fadd_rn(a2.y, b1));
+                amax = fmaxf(amax, fmaxf(fabsf(a2.x), fabsf(a2.y)));
+            }
+            const float inv = q8_inv_scale(amax);
+            p.d_out[(kb_out0 + blk) * p.d_ld + m] = q8_scale(amax);
+            if constexpr (kOps == kOpsF16) {
+                __half* qrow = reinterpret_cast<__half*>(p.q_out) + static_cast<int64_t>(m) * p.Kp_out + n0;
+#pragma unroll
+                for (int i = 0; i < 32; i += 8) {
+                    __half2 h[4];
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        h[t] = __halves2half2(__int2half_rn(q8_round(acc[blk * 16 + i / 2 + t].x, inv)),
+                                              __int2half_rn(q8_round(acc[blk * 16 + i / 2 + t].y, inv)));
+                    *reinterpret_cast<uint4*>(qrow + i) = *reinterpret_cast<uint4*>(h);
+                }
+            } else {
+                int8_t* qrow = reinterpret_cast<int8_t*>(p.q_out) + static_cast<int64_t>(m) * p.Kp_out + n0;
+#pragma unroll
+                for (int i = 0; i < 32; i += 16) {
+                    uint32_t wv[4];
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        uint32_t b = 0;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int col = i + 4 * t + e;
+                            const float2 a2 = acc[blk * 16 + col / 2];
+                            b |= (static_cast<uint32_t>(q8_round((col & 1) ? a2.y : a2.x, inv)) & 0xFFu) << (8 * e);
+                        }
+                        wv[t] = b;
+                    }
+                    *reinterpret_cast<uint4*>(qrow + i) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                }
+            }
+        }
+    } else if (p.epi == B2Q_EPI_BIAS_F16) {
+        __half* orow = reinterpret_cast<__half*>(p.out) + static_cast<int64_t>(m) * p.ld_out;
+#pragma unroll
+        for (int i = 0; i < Cfg::COLS / 2; i += 2) {
+            const int n = nbase + 2 * i;
+            if (n < p.N) {
+                const float4 b = p.bias ? *reinterpret_cast<const float4*>(p.bias + n) : make_float4(0, 0, 0, 0);
+                __half2 h0 = __floats2half2_rn(__fadd_rn(acc[i].x, b.x), __fadd_rn(acc[i].y, b.y));
+                __half2 h1 = __floats2half2_rn(__fadd_rn(acc[i + 1].x, b.z), __fadd_rn(acc[i + 1].y, b.w));
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&h0);
+                u.y = *reinterpret_cast<uint32_t*>(&h1);
+                *reinterpret_cast<uint2*>(orow + n) = u;
+            }
+        }
+    } else {
+        float* orow = reinterpret_cast<float*>(p.out) + static_cast<int64_t>(m) * p.ld_out;
+        const float* rrow = p.residual ? p.residual + static_cast<int64_t>(m) * p.ld_out : nullptr;
+#pragma unroll
+        for (int i = 0; i < Cfg::COLS / 2; i += 2) {
+            const int n = nbase + 2 * i;
+            if (n < p.N) {
+                float4 v = make_float4(acc[i].x, acc[i].y, acc[i + 1].x, acc[i + 1].y);
+                if (p.epi != B2Q_EPI_NONE && p.bias) {
+                    const float4 b = *reinterpret_cast<const float4*>(p.bias + n);
+                    v.x = __fadd_rn(v.x, b.x);
+                    v.y = __fadd_rn(v.y, b.y);
+                    v.z = __fadd_rn(v.z, b.z);
+                    v.w = __fadd_rn(v.w, b.w);
+                }
+                if (p.epi == B2Q_EPI_BIAS_RESIDUAL) {
+                    const float4 r = *reinterpret_cast<const float4*>(rrow + n);
+                    v.x = __fadd_rn(v.x, r.x);
+                    v.y = __fadd_rn(v.y, r.y);
+                    v.z = __fadd_rn(v.z, r.z);
+                    v.w = __fadd_rn(v.w, r.w);
+                }
+                *reinterpret_cast<float4*>(orow + n) = v;
+            }
+        }
+    }
+}
+
+template <int kOps, int kBN, bool kDump>
+__device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParams& p, int warp, int lane) {
+    using Cfg = GemmCfg<kOps, kBN>;
+    const int ew = warp - 4;
+    const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
+    const int half = ew >> 2;                   // which BN/2 column half
+    const int row = quad * 32 + lane;           // row inside the tile
+    const int col0 = half * Cfg::COLS;
+    const uint32_t taddr0 = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + col0;
+    const int num_tiles = p.m_tiles * p.n_tiles;
+    const int nst = (p.Kb + Cfg::KBS - 1) / Cfg::KBS;
+    Ring<Cfg::STAGES> st_ring;
+    Ring<Cfg::NBUF> acc_ring;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles;
+        const int m = mb * Cfg::BM + row;
+        const int nbase = nb * Cfg::BN + col0;
+        float2 acc[Cfg::COLS / 2];
+#pragma unroll
+        for (int i = 0; i < Cfg::COLS / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
+        uint32_t ra[32], rb[32];
+        if (!mbar_wait(&sm.tfull[acc_ring.idx], acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
+            raise_error(p.err, sm.abort_flag, kDevTimeoutTmemFull);
+            return false;
+        }
+        tc_fence_after();
+        tmem_ld_32x32b_x32(taddr0 + acc_ring.idx * Cfg::BN, ra);
+        int kb = 0;
+        for (int st = 0; st < nst; ++st) {
+            const uint32_t s = st_ring.idx;
+            if (!mbar_wait(&sm.full[s], st_ring.phase, sm.abort_flag, p.timeout_ns)) {
+                raise_error(p.err, sm.abort_flag, kDevTimeoutFull);
+                return false;
+            }
+            const uint8_t* sbase = sm.base + s * Cfg::STAGE_BYTES;
+            const float* sdx = reinterpret_cast<const float*>(sbase + Cfg::A_BYTES + Cfg::B_BYTES) + row;
+            const float4* sdw =
+                reinterpret_cast<const float4*>(sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES) + col0 / 4;
+            const int nkb = min(Cfg::KBS, p.Kb - st * Cfg::KBS);
+#pragma unroll
+            for (int j = 0; j < Cfg::KBS; ++j) {
+                if (j < nkb) {
+                    const float dx = sdx[j * Cfg::BM];
+                    const float2 dx2 = make_float2(dx, dx);
+                    const float4* w4 = sdw + j * (Cfg::BN / 4);
+                    const bool has_next = kb + 1 < p.Kb;
+#pragma unroll
+                    for (int c = 0; c < Cfg::CH; ++c) {
+                        uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+                        uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+                        tmem_ld_wait_regs(cur);
+                        if (c == Cfg::CH - 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&sm.tempty[acc_ring.idx]);
+                            acc_ring.next();
+                            if (has_next) {
+                                if (!mbar_wait(&sm.tfull[acc_ring.idx], acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
+                                    raise_error(p.err, sm.abort_flag, kDevTimeoutTmemFull);
+                                    return false;
+                                }
+                                tc_fence_after();
+                                tmem_ld_32x32b_x32(taddr0 + acc_ring.idx * Cfg::BN, nxt);
+                            }
+                        } else {
+                            tmem_ld_32x32b_x32(taddr0 + acc_ring.idx * Cfg::BN + (c + 1) * 32, nxt);
+                        }
+                        if constexpr (kDump) {
+                            if (m < p.M) {
+                                int32_t* drow = p.dump + (static_cast<int64_t>(kb) * p.M + m) * p.N;
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) {
+                                    const int n = nbase + c * 32 + i;
+                                    if (n < p.N) drow[n] = static_cast<int32_t>(carrier_to_float<kOps>(cur[i]));
+                                }
+                            }
+                        } else {
+                            rescale_chunk<kOps>(acc + c * 16, cur, w4 + c * 8, dx2);
+                        }
+                    }
+                    ++kb;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[s]);
+            st_ring.next();
+        }
+        if constexpr (!kDump) store_tile<kOps, kBN>(p, acc, m, nbase);
+    }
+    return true;
 }
 
 template <int kOps, int kBN, bool kDump>
@@ -116,28 +401,29 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                const GemmParams p) {
     using Cfg = GemmCfg<kOps, kBN>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
-    uint64_t* full = bars;                           // [STAGES] TMA landed
-    uint64_t* empty = bars + Cfg::STAGES;            // [STAGES] MMA + epilogue done with the stage
-    uint64_t* tfull = bars + 2 * Cfg::STAGES;        // [NBUF]   accumulator ready
-    uint64_t* tempty = tfull + Cfg::NBUF;            // [NBUF]   accumulator drained
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + Cfg::NBUF);
-    volatile uint32_t* abort_flag = tmem_slot + 1;
+    Smem sm;
+    sm.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm.base + Cfg::STAGES * Cfg::STAGE_BYTES);
+    sm.full = bars;                          // [STAGES] TMA landed
+    sm.empty = bars + Cfg::STAGES;           // [STAGES] MMA + epilogue done with the stage
+    sm.tfull = bars + 2 * Cfg::STAGES;       // [NBUF]   accumulator ready
+    sm.tempty = sm.tfull + Cfg::NBUF;        // [NBUF]   accumulator drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm.tempty + Cfg::NBUF);
+    sm.abort_flag = tmem_slot + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1 + Cfg::EPI_WARPS);
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1 + Cfg::EPI_WARPS);
         }
         for (int b = 0; b < Cfg::NBUF; ++b) {
-            mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], Cfg::EPI_WARPS);
+            mbar_init(&sm.tfull[b], 1);
+            mbar_init(&sm.tempty[b], Cfg::EPI_WARPS);
         }
-        *abort_flag = 0u;
+        *sm.abort_flag = 0u;
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -148,268 +434,35 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int num_tiles = p.m_tiles * p.n_tiles;
-    const int nst = (p.Kb + Cfg::KBS - 1) / Cfg::KBS;
-
     if (warp < 4) {
         warpgroup_reg_dealloc<Cfg::WG0_REGS>();
         if (warp == 0 && lane == 0) {
-            // ------------------------------------------------------------ producer
             tma_prefetch_desc(&tmA);
             tma_prefetch_desc(&tmB);
             tma_prefetch_desc(&tmDX);
             tma_prefetch_desc(&tmDW);
-            uint32_t gs = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int mb = tile / p.n_tiles, nb = tile % p.n_tiles;
-                for (int st = 0; st < nst; ++st, ++gs) {
-                    const uint32_t slot = gs % Cfg::STAGES, ph = (gs / Cfg::STAGES) & 1u;
-                    if (!mbar_wait(&empty[slot], ph ^ 1u, abort_flag, p.timeout_ns)) {
-                        raise_error(p.err, abort_flag, kDevTimeoutEmpty);
-                        ok = false;
-                        break;
-                    }
-                    uint8_t* sbase = smem + slot * Cfg::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[slot], Cfg::STAGE_BYTES);
-                    const int kx = st * (Cfg::KROW / Cfg::ES);
-                    tma_load_2d(sbase, &tmA, &full[slot], kx, mb * Cfg::BM);
-                    tma_load_2d(sbase + Cfg::A_BYTES, &tmB, &full[slot], kx, nb * Cfg::BN);
-                    tma_load_2d(sbase + Cfg::A_BYTES + Cfg::B_BYTES, &tmDX, &full[slot], mb * Cfg::BM,
-                                st * Cfg::KBS);
-                    tma_load_2d(sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES, &tmDW, &full[slot],
-                                nb * Cfg::BN, st * Cfg::KBS);
-                }
-            }
+            uint32_t issued = 0;
+            run_producer<kOps, kBN>(sm, &tmA, &tmB, &tmDX, &tmDW, p, issued);
             // drain: never leave a copy in flight into this CTA's shared memory
-            const uint32_t n_drain = gs < Cfg::STAGES ? gs : Cfg::STAGES;
+            const uint32_t n_drain = issued < Cfg::STAGES ? issued : Cfg::STAGES;
             for (uint32_t i = 0; i < n_drain; ++i) {
-                const uint32_t g = gs - 1 - i;
+                const uint32_t g = issued - 1 - i;
                 volatile uint32_t no_abort = 0;
-                mbar_wait(&full[g % Cfg::STAGES], (g / Cfg::STAGES) & 1u, &no_abort, 100000000ull);
+                mbar_wait(&sm.full[g % Cfg::STAGES], (g / Cfg::STAGES) & 1u, &no_abort, 100000000ull);
             }
         } else if (warp == 1 && lane == 0) {
-            // ------------------------------------------------------------ MMA issuer
-            const uint32_t idesc =
-                kOps == kOpsF16 ? idesc_f16_f32(Cfg::BM, Cfg::BN) : idesc_i8_s32(Cfg::BM, Cfg::BN);
-            uint32_t gs = 0, gk = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                for (int st = 0; st < nst && ok; ++st, ++gs) {
-                    const uint32_t slot = gs % Cfg::STAGES, ph = (gs / Cfg::STAGES) & 1u;
-                    if (!mbar_wait(&full[slot], ph, abort_flag, p.timeout_ns)) {
-                        raise_error(p.err, abort_flag, kDevTimeoutFull);
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_base = smem_u32(smem + slot * Cfg::STAGE_BYTES);
-                    const uint32_t b_base = a_base + Cfg::A_BYTES;
-                    for (int j = 0; j < Cfg::KBS; ++j) {
-                        const int kb = st * Cfg::KBS + j;
-                        if (kb >= p.Kb) break;
-                        const uint32_t buf = gk % Cfg::NBUF, tph = (gk / Cfg::NBUF) & 1u;
-                        if (!mbar_wait(&tempty[buf], tph ^ 1u, abort_flag, p.timeout_ns)) {
-                            raise_error(p.err, abort_flag, kDevTimeoutTmemEmpty);
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t d = tmem_base + buf * Cfg::BN;
-                        if constexpr (kOps == kOpsF16) {
-                            mma_f16(d, smem_desc_k_sw128(a_base + j * 64), smem_desc_k_sw128(b_base + j * 64), idesc,
-                                    0u);
-                            mma_f16(d, smem_desc_k_sw128(a_base + j * 64 + 32),
-                                    smem_desc_k_sw128(b_base + j * 64 + 32), idesc, 1u);
-                        } else {
-                            mma_i8(d, smem_desc_k_sw128(a_base + j * 32), smem_desc_k_sw128(b_base + j * 32), idesc,
-                                   0u);
-                        }
-                        mma_commit(&tfull[buf]);
-                        ++gk;
-                    }
-                    mma_commit(&empty[slot]);
-                }
-            }
+            uint32_t issued = 0;
+            run_mma<kOps, kBN>(sm, tmem_base, p, issued);
             // every issued MMA must have retired before TMEM is released
-            if (gk > 0) {
+            if (issued > 0) {
                 volatile uint32_t no_abort = 0;
-                const uint32_t g = gk - 1;
-                mbar_wait(&tfull[g % Cfg::NBUF], (g / Cfg::NBUF) & 1u, &no_abort, 100000000ull);
+                const uint32_t g = issued - 1;
+                mbar_wait(&sm.tfull[g % Cfg::NBUF], (g / Cfg::NBUF) & 1u, &no_abort, 100000000ull);
             }
         }
     } else {
         warpgroup_reg_alloc<Cfg::EPI_REGS>();
-        // ------------------------------------------------------------ epilogue
-        const int ew = warp - 4;
-        const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
-        const int part = ew >> 2;                   // which BN/4 column quarter
-        const int row = quad * 32 + lane;           // row inside the tile
-        const int col0 = part * Cfg::COLS;
-        const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-        uint32_t gs = 0, gk = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-            const int mb = tile / p.n_tiles, nb = tile % p.n_tiles;
-            const int m = mb * Cfg::BM + row;
-            const int nbase = nb * Cfg::BN + col0;
-            float2 acc[Cfg::COLS / 2];
-#pragma unroll
-            for (int i = 0; i < Cfg::COLS / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
-
-            for (int st = 0; st < nst && ok; ++st) {
-                const uint32_t g = gs + st;
-                const uint32_t slot = g % Cfg::STAGES, ph = (g / Cfg::STAGES) & 1u;
-                if (!mbar_wait(&full[slot], ph, abort_flag, p.timeout_ns)) {
-                    raise_error(p.err, abort_flag, kDevTimeoutFull);
-                    ok = false;
-                    break;
-                }
-                const uint8_t* sbase = smem + slot * Cfg::STAGE_BYTES;
-                const float* sdx = reinterpret_cast<const float*>(sbase + Cfg::A_BYTES + Cfg::B_BYTES);
-                const float* sdw = reinterpret_cast<const float*>(sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES);
-                for (int j = 0; j < Cfg::KBS && ok; ++j) {
-                    const int kb = st * Cfg::KBS + j;
-                    if (kb >= p.Kb) break;
-                    const uint32_t buf = gk % Cfg::NBUF, tph = (gk / Cfg::NBUF) & 1u;
-                    if (!mbar_wait(&tfull[buf], tph, abort_flag, p.timeout_ns)) {
-                        raise_error(p.err, abort_flag, kDevTimeoutTmemFull);
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const float dx = sdx[j * Cfg::BM + row];
-                    const float2 dx2 = make_float2(dx, dx);
-                    const float4* w4 = reinterpret_cast<const float4*>(sdw + j * Cfg::BN + col0);
-#pragma unroll
-                    for (int c = 0; c < Cfg::CH; ++c) {
-                        uint64_t r[16];
-                        tmem_ld_32x32b_x32_pairs(tmem_base + lane_addr + buf * Cfg::BN + col0 + c * 32, r);
-                        if (c == Cfg::CH - 1) {
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&tempty[buf]);
-                        }
-                        if constexpr (kDump) {
-                            if (m < p.M) {
-                                int32_t* drow = p.dump + (static_cast<int64_t>(kb) * p.M + m) * p.N;
-#pragma unroll
-                                for (int i = 0; i < 32; ++i) {
-                                    const int n = nbase + c * 32 + i;
-                                    const uint32_t v = static_cast<uint32_t>(r[i / 2] >> (32 * (i & 1)));
-                                    if (n < p.N) drow[n] = static_cast<int32_t>(carrier_to_float<kOps>(v));
-                                }
-                            }
-                        } else {
-                            rescale_chunk<kOps>(acc + c * 16, r, w4 + c * 8, dx2);
-                        }
-                    }
-                    ++gk;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
-            }
-            gs += nst;
-            if (!ok || kDump) continue;
-
-            // ---------------------------------------------------- tile epilogue
-            if (m < p.M) {
-                if (p.epi == B2Q_EPI_BIAS_GELU_Q8) {
-                    const int64_t kb_out0 = nbase / 32;
-#pragma unroll
-                    for (int blk = 0; blk < Cfg::COLS / 32; ++blk) {
-                        const int n0 = nbase + blk * 32;
-                        if (n0 >= p.Kp_out) break;
-                        float amax = 0.0f;
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const int n = n0 + 2 * i;
-                            const float b0 = (p.bias && n < p.N) ? p.bias[n] : 0.0f;
-                            const float b1 = (p.bias && n + 1 < p.N) ? p.bias[n + 1] : 0.0f;
-                            float2& a2 = acc[blk * 16 + i];
-                            a2.x = gelu_tanh(__fadd_rn(a2.x, b0));
-                            a2.y = gelu_tanh(__fadd_rn(a2.y, b1));
-                            amax = fmaxf(amax, fmaxf(fabsf(a2.x), fabsf(a2.y)));
-                        }
-                        const float inv = q8_inv_scale(amax);
-                        p.d_out[(kb_out0 + blk) * p.d_ld + m] = q8_scale(amax);
-                        if constexpr (kOps == kOpsF16) {
-                            __half* qrow = reinterpret_cast<__half*>(p.q_out) + static_cast<int64_t>(m) * p.Kp_out + n0;
-#pragma unroll
-                            for (int i = 0; i < 32; i += 8) {
-                                __half2 h[4];
-#pragma unroll
-                                for (int t = 0; t < 4; ++t)
-                                    h[t] = __halves2half2(__int2half_rn(q8_round(acc[blk * 16 + i / 2 + t].x, inv)),
-                                                          __int2half_rn(q8_round(acc[blk * 16 + i / 2 + t].y, inv)));
-                                *reinterpret_cast<uint4*>(qrow + i) = *reinterpret_cast<uint4*>(h);
-                            }
-                        } else {
-                            int8_t* qrow = reinterpret_cast<int8_t*>(p.q_out) + static_cast<int64_t>(m) * p.Kp_out + n0;
-#pragma unroll
-                            for (int i = 0; i < 32; i += 16) {
-                                uint32_t wv[4];
-#pragma unroll
-                                for (int t = 0; t < 4; ++t) {
-                                    uint32_t b = 0;
-#pragma unroll
-                                    for (int e = 0; e < 4; ++e) {
-                                        const int col = i + 4 * t + e;
-                                        const float2 a2 = acc[blk * 16 + col / 2];
-                                        b |= (static_cast<uint32_t>(q8_round((col & 1) ? a2.y : a2.x, inv)) & 0xFFu)
-                                             << (8 * e);
-                                    }
-                                    wv[t] = b;
-                                }
-                                *reinterpret_cast<uint4*>(qrow + i) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-                            }
-                        }
-                    }
-                } else if (p.epi == B2Q_EPI_BIAS_F16) {
-                    __half* orow = reinterpret_cast<__half*>(p.out) + static_cast<int64_t>(m) * p.ld_out;
-#pragma unroll
-                    for (int i = 0; i < Cfg::COLS / 2; i += 2) {
-                        const int n = nbase + 2 * i;
-                        if (n < p.N) {
-                            const float4 b =
-                                p.bias ? *reinterpret_cast<const float4*>(p.bias + n) : make_float4(0, 0, 0, 0);
-                            __half2 h0 = __floats2half2_rn(__fadd_rn(acc[i].x, b.x), __fadd_rn(acc[i].y, b.y));
-                            __half2 h1 =
-                                __floats2half2_rn(__fadd_rn(acc[i + 1].x, b.z), __fadd_rn(acc[i + 1].y, b.w));
-                            uint2 u;
-                            u.x = *reinterpret_cast<uint32_t*>(&h0);
-                            u.y = *reinterpret_cast<uint32_t*>(&h1);
-                            *reinterpret_cast<uint2*>(orow + n) = u;
-                        }
-                    }
-                } else {
-                    float* orow = reinterpret_cast<float*>(p.out) + static_cast<int64_t>(m) * p.ld_out;
-                    const float* rrow = p.residual ? p.residual + static_cast<int64_t>(m) * p.ld_out : nullptr;
-#pragma unroll
-                    for (int i = 0; i < Cfg::COLS / 2; i += 2) {
-                        const int n = nbase + 2 * i;
-                        if (n < p.N) {
-                            float4 v = make_float4(acc[i].x, acc[i].y, acc[i + 1].x, acc[i + 1].y);
-                            if (p.epi != B2Q_EPI_NONE && p.bias) {
-                                const float4 b = *reinterpret_cast<const float4*>(p.bias + n);
-                                v.x = __fadd_rn(v.x, b.x);
-                                v.y = __fadd_rn(v.y, b.y);
-                                v.z = __fadd_rn(v.z, b.z);
-                                v.w = __fadd_rn(v.w, b.w);
-                            }
-                            if (p.epi == B2Q_EPI_BIAS_RESIDUAL) {
-                                const float4 r = *reinterpret_cast<const float4*>(rrow + n);
-                                v.x = __fadd_rn(v.x, r.x);
-                                v.y = __fadd_rn(v.y, r.y);
-                                v.z = __fadd_rn(v.z, r.z);
-                                v.w = __fadd_rn(v.w, r.w);
-                            }
-                            *reinterpret_cast<float4*>(orow + n) = v;
-                        }
-                    }
-                }
-            }
-        }
+        run_epilogue<kOps, kBN, kDump>(sm, tmem_base, p, warp, lane);
         tc_fence_before();
     }
 
@@ -486,9 +539,7 @@ static b2q_status dispatch_bn(const GemmArgs& a, cudaStream_t s, int bn) {
 
 b2q_status launch_gemm(const GemmArgs& a, cudaStream_t s) {
     DeviceState* ds = state();
-    // 128-column tiles by default: with sixteen epilogue warps the 256-wide
-    // tile does not fit the epilogue's register share.
-    const int bn = ds->gemm_bn == 256 ? 256 : 128;
+    const int bn = ds->gemm_bn == 128 ? 128 : 256;
     return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, bn) : dispatch_bn<kOpsI8>(a, s, bn);
 }
 
