@@ -50,7 +50,8 @@ struct GemmCfg {
     static constexpr int WG0_REGS = 56;                    // 128*56 + 256*224 = 384*168
     static constexpr int EPI_REGS = 224;
     static constexpr int COLS = BN / 2;                    // columns per epilogue thread
-    static constexpr int CH = COLS / 32;                   // 32-column TMEM loads per K block
+    static constexpr int CC = COLS / 64;                   // 64-column chunks per epilogue thread
+    static constexpr int CH = 2 * CC;                      // 16x256b.x8 TMEM loads per K block (2 slabs)
     static constexpr int NBUF = 512 / BN;                  // accumulator ring depth (power of two)
     static constexpr int TMEM_COLS = 512;
     static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment for the swizzle");
@@ -90,18 +91,17 @@ __device__ __forceinline__ float carrier_to_float(uint32_t r) {
     }
 }
 
-// acc[i] (i < 16) += ((float)S * dW) * dX for the 32 columns of one chunk.
+// One 16x256b.x8 chunk: 2 rows (lane t/4 and t/4 + 8 of a 16-lane slab) x
+// 8 column pairs.  acc[2g + h] += ((float)S * dW) * dX for row h, pair g.
 template <int kOps>
-__device__ __forceinline__ void rescale_chunk(float2* acc, const uint32_t (&r)[32], const float4* w4, float2 dx2) {
+__device__ __forceinline__ void rescale_chunk(float2* acc, const uint32_t (&r)[32], const float2 (&w2)[8], float2 dx0,
+                                              float2 dx1) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 w = w4[i];
-        const float2 f01 = make_float2(carrier_to_float<kOps>(r[4 * i + 0]), carrier_to_float<kOps>(r[4 * i + 1]));
-        const float2 f23 = make_float2(carrier_to_float<kOps>(r[4 * i + 2]), carrier_to_float<kOps>(r[4 * i + 3]));
-        const float2 t01 = __fmul2_rn(f01, make_float2(w.x, w.y));
-        const float2 t23 = __fmul2_rn(f23, make_float2(w.z, w.w));
-        acc[2 * i] = __ffma2_rn(t01, dx2, acc[2 * i]);
-        acc[2 * i + 1] = __ffma2_rn(t23, dx2, acc[2 * i + 1]);
+    for (int g = 0; g < 8; ++g) {
+        const float2 f0 = make_float2(carrier_to_float<kOps>(r[4 * g + 0]), carrier_to_float<kOps>(r[4 * g + 1]));
+        const float2 f1 = make_float2(carrier_to_float<kOps>(r[4 * g + 2]), carrier_to_float<kOps>(r[4 * g + 3]));
+        acc[2 * g] = __ffma2_rn(__fmul2_rn(f0, w2[g]), dx0, acc[2 * g]);
+        acc[2 * g + 1] = __ffma2_rn(__fmul2_rn(f1, w2[g]), dx1, acc[2 * g + 1]);
     }
 }
 
@@ -117,14 +117,18 @@ struct Ring {
     }
 };
 
+// Shared-memory layout, as 32-bit shared-window addresses: the stages, then
+// the barrier arrays (8 bytes per barrier).
 struct Smem {
-    uint8_t* base;
-    uint64_t* full;
-    uint64_t* empty;
-    uint64_t* tfull;
-    uint64_t* tempty;
+    uint32_t base;
+    uint32_t full;      // [STAGES] TMA landed
+    uint32_t empty;     // [STAGES] MMA + epilogue done with the stage
+    uint32_t tfull;     // [NBUF]   accumulator ready
+    uint32_t tempty;    // [NBUF]   accumulator drained
     volatile uint32_t* abort_flag;
 };
+
+__device__ __forceinline__ uint32_t bar_at(uint32_t arr, uint32_t i) { return arr + 8u * i; }
 
 // ---------------------------------------------------------------- producer
 template <int kOps, int kBN>
@@ -138,18 +142,18 @@ __device__ bool run_producer(const Smem& sm, const CUtensorMap* tmA, const CUten
         const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles;
         for (int st = 0; st < nst; ++st) {
             const uint32_t s = st_ring.idx;
-            if (!mbar_wait(&sm.empty[s], st_ring.phase ^ 1u, sm.abort_flag, p.timeout_ns)) {
+            if (!mbar_wait(bar_at(sm.empty, s), st_ring.phase ^ 1u, sm.abort_flag, p.timeout_ns)) {
                 raise_error(p.err, sm.abort_flag, kDevTimeoutEmpty);
                 return false;
             }
-            uint8_t* sbase = sm.base + s * Cfg::STAGE_BYTES;
-            mbar_arrive_expect_tx(&sm.full[s], Cfg::STAGE_BYTES);
+            const uint32_t sbase = sm.base + s * Cfg::STAGE_BYTES;
+            const uint32_t fb = bar_at(sm.full, s);
+            mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
             const int kx = st * (Cfg::KROW / Cfg::ES);
-            tma_load_2d(sbase, tmA, &sm.full[s], kx, mb * Cfg::BM);
-            tma_load_2d(sbase + Cfg::A_BYTES, tmB, &sm.full[s], kx, nb * Cfg::BN);
-            tma_load_2d(sbase + Cfg::A_BYTES + Cfg::B_BYTES, tmDX, &sm.full[s], mb * Cfg::BM, st * Cfg::KBS);
-            tma_load_2d(sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES, tmDW, &sm.full[s], nb * Cfg::BN,
-                        st * Cfg::KBS);
+            tma_load_2d(sbase, tmA, fb, kx, mb * Cfg::BM);
+            tma_load_2d(sbase + Cfg::A_BYTES, tmB, fb, kx, nb * Cfg::BN);
+            tma_load_2d(sbase + Cfg::A_BYTES + Cfg::B_BYTES, tmDX, fb, mb * Cfg::BM, st * Cfg::KBS);
+            tma_load_2d(sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES, tmDW, fb, nb * Cfg::BN, st * Cfg::KBS);
             ++issued;
             st_ring.next();
         }
@@ -169,17 +173,17 @@ __device__ bool run_mma(const Smem& sm, uint32_t tmem_base, const GemmParams& p,
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
         for (int st = 0; st < nst; ++st) {
             const uint32_t s = st_ring.idx;
-            if (!mbar_wait(&sm.full[s], st_ring.phase, sm.abort_flag, p.timeout_ns)) {
+            if (!mbar_wait(bar_at(sm.full, s), st_ring.phase, sm.abort_flag, p.timeout_ns)) {
                 raise_error(p.err, sm.abort_flag, kDevTimeoutFull);
                 return false;
             }
             tc_fence_after();
-            const uint32_t a_base = smem_u32(sm.base + s * Cfg::STAGE_BYTES);
+            const uint32_t a_base = sm.base + s * Cfg::STAGE_BYTES;
             const uint32_t b_base = a_base + Cfg::A_BYTES;
             const int nkb = min(Cfg::KBS, p.Kb - st * Cfg::KBS);
             for (int j = 0; j < nkb; ++j) {
                 const uint32_t b = acc_ring.idx;
-                if (!mbar_wait(&sm.tempty[b], acc_ring.phase ^ 1u, sm.abort_flag, p.timeout_ns)) {
+                if (!mbar_wait(bar_at(sm.tempty, b), acc_ring.phase ^ 1u, sm.abort_flag, p.timeout_ns)) {
                     raise_error(p.err, sm.abort_flag, kDevTimeoutTmemEmpty);
                     return false;
                 }
@@ -192,11 +196,11 @@ __device__ bool run_mma(const Smem& sm, uint32_t tmem_base, const GemmParams& p,
                 } else {
                     mma_i8(d, smem_desc_k_sw128(a_base + j * 32), smem_desc_k_sw128(b_base + j * 32), idesc, 0u);
                 }
-                mma_commit(&sm.tfull[b]);
+                mma_commit(bar_at(sm.tfull, b));
                 ++issued;
                 acc_ring.next();
             }
-            mma_commit(&sm.empty[s]);
+            mma_commit(bar_at(sm.empty, s));
             st_ring.next();
         }
     }
@@ -204,99 +208,124 @@ __device__ bool run_mma(const Smem& sm, uint32_t tmem_base, const GemmParams& p,
 }
 
 // ---------------------------------------------------------------- epilogue
+//
+// Thread geometry.  Epilogue warp ew (0..7) reads TMEM lane quadrant
+// quad = warp % 4 (the only lanes a warp may access) and column half
+// ew / 4 of the tile, through 16x256b loads: lane t holds rows
+// quad*32 + 16s + t/4 + 8h (slab s, h in {0,1}) and the column pairs
+// 64cc + 8g + 2(t%4) + {0,1} of its half (64-column chunk cc, pair g < 8).
+// Chunk c = 2cc + s is one 32-register load; acc[16c + 2g + h] is the pair
+// (g, h).  Holding four rows and 32 columns (instead of one row and all 128
+// columns) makes each shared-memory scale load serve four rows, which keeps
+// the per-block rescale off the shared-memory pipe.
+
 template <int kOps, int kBN>
-__device__ __forceinline__ void store_tile(const GemmParams& p, float2 (&acc)[GemmCfg<kOps, kBN>::COLS / 2], int m,
-                                           int nbase) {
+__device__ __forceinline__ void store_tile(const GemmParams& p, float2* acc, int mrow0, int nblk0, int q) {
     using Cfg = GemmCfg<kOps, kBN>;
-    if (m >= p.M) return;
     if (p.epi == B2Q_EPI_BIAS_GELU_Q8) {
-        const int64_t kb_out0 = nbase / 32;
 #pragma unroll
-        for (int blk = 0; blk < Cfg::COLS / 32; ++blk) {
-            const int n0 = nbase + blk * 32;
-            if (n0 >= p.Kp_out) break;
-            float amax = 0.0f;
+        for (int cc = 0; cc < Cfg::CC; ++cc) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int n = n0 + 2 * i;
-                const float b0 = (p.bias && n < p.N) ? p.bias[n] : 0.0f;
-                const float b1 = (p.bias && n + 1 < p.N) ? p.bias[n + 1] : 0.0f;
-                float2& a2 = acc[blk * 16 + i];
-                a2.x = gelu_tanh(__fadd_rn(a2.x, b0));
-                a2.y = gelu_tanh(__fadd_rn(a2.y, b1));
-                amax = fmaxf(amax, fmaxf(fabsf(a2.x), fabsf(a2.y)));
-            }
-            const float inv = q8_inv_scale(amax);
-            p.d_out[(kb_out0 + blk) * p.d_ld + m] = q8_scale(amax);
-            if constexpr (kOps == kOpsF16) {
-                __half* qrow = reinterpret_cast<__half*>(p.q_out) + static_cast<int64_t>(m) * p.Kp_out + n0;
+            for (int bl = 0; bl < 2; ++bl) {
+                const int n0 = nblk0 + cc * 64 + bl * 32;        // q8_1 block start (warp-uniform)
+                if (n0 >= p.Kp_out) continue;
+                float2 b2[4];
 #pragma unroll
-                for (int i = 0; i < 32; i += 8) {
-                    __half2 h[4];
-#pragma unroll
-                    for (int t = 0; t < 4; ++t)
-                        h[t] = __halves2half2(__int2half_rn(q8_round(acc[blk * 16 + i / 2 + t].x, inv)),
-                                              __int2half_rn(q8_round(acc[blk * 16 + i / 2 + t].y, inv)));
-                    *reinterpret_cast<uint4*>(qrow + i) = *reinterpret_cast<uint4*>(h);
+                for (int gg = 0; gg < 4; ++gg) {
+                    const int n = n0 + 8 * gg + 2 * q;
+                    b2[gg] = (p.bias && n < p.N) ? *reinterpret_cast<const float2*>(p.bias + n) : make_float2(0.0f, 0.0f);
                 }
-            } else {
-                int8_t* qrow = reinterpret_cast<int8_t*>(p.q_out) + static_cast<int64_t>(m) * p.Kp_out + n0;
 #pragma unroll
-                for (int i = 0; i < 32; i += 16) {
-                    uint32_t wv[4];
+                for (int s = 0; s < 2; ++s) {
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        uint32_t b = 0;
+                    for (int h = 0; h < 2; ++h) {
+                        float2 v[4];
+                        float amax = 0.0f;
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int col = i + 4 * t + e;
-                            const float2 a2 = acc[blk * 16 + col / 2];
-                            b |= (static_cast<uint32_t>(q8_round((col & 1) ? a2.y : a2.x, inv)) & 0xFFu) << (8 * e);
+                        for (int gg = 0; gg < 4; ++gg) {
+                            const float2 a = acc[16 * (2 * cc + s) + 2 * (4 * bl + gg) + h];
+                            v[gg].x = gelu_tanh(__fadd_rn(a.x, b2[gg].x));
+                            v[gg].y = gelu_tanh(__fadd_rn(a.y, b2[gg].y));
+                            amax = fmaxf(amax, fmaxf(fabsf(v[gg].x), fabsf(v[gg].y)));
                         }
-                        wv[t] = b;
+                        // the block's 32 values of this row sit in the 4 lanes sharing t/4
+                        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                        const int m = mrow0 + 16 * s + 8 * h;
+                        if (m < p.M) {
+                            if (q == 0) p.d_out[static_cast<int64_t>(n0 / 32) * p.d_ld + m] = q8_scale(amax);
+                            const float inv = q8_inv_scale(amax);
+#pragma unroll
+                            for (int gg = 0; gg < 4; ++gg) {
+                                const int64_t off = static_cast<int64_t>(m) * p.Kp_out + n0 + 8 * gg + 2 * q;
+                                if constexpr (kOps == kOpsF16) {
+                                    reinterpret_cast<__half2*>(reinterpret_cast<__half*>(p.q_out) + off)[0] =
+                                        __halves2half2(__int2half_rn(q8_round(v[gg].x, inv)),
+                                                       __int2half_rn(q8_round(v[gg].y, inv)));
+                                } else {
+                                    const uint32_t lo = static_cast<uint32_t>(q8_round(v[gg].x, inv)) & 0xFFu;
+                                    const uint32_t hi = static_cast<uint32_t>(q8_round(v[gg].y, inv)) & 0xFFu;
+                                    reinterpret_cast<uint16_t*>(reinterpret_cast<int8_t*>(p.q_out) + off)[0] =
+                                        static_cast<uint16_t>(lo | (hi << 8));
+                                }
+                            }
+                        }
                     }
-                    *reinterpret_cast<uint4*>(qrow + i) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
             }
         }
     } else if (p.epi == B2Q_EPI_BIAS_F16) {
-        __half* orow = reinterpret_cast<__half*>(p.out) + static_cast<int64_t>(m) * p.ld_out;
+        __half* out = reinterpret_cast<__half*>(p.out);
 #pragma unroll
-        for (int i = 0; i < Cfg::COLS / 2; i += 2) {
-            const int n = nbase + 2 * i;
-            if (n < p.N) {
-                const float4 b = p.bias ? *reinterpret_cast<const float4*>(p.bias + n) : make_float4(0, 0, 0, 0);
-                __half2 h0 = __floats2half2_rn(__fadd_rn(acc[i].x, b.x), __fadd_rn(acc[i].y, b.y));
-                __half2 h1 = __floats2half2_rn(__fadd_rn(acc[i + 1].x, b.z), __fadd_rn(acc[i + 1].y, b.w));
-                uint2 u;
-                u.x = *reinterpret_cast<uint32_t*>(&h0);
-                u.y = *reinterpret_cast<uint32_t*>(&h1);
-                *reinterpret_cast<uint2*>(orow + n) = u;
+        for (int cc = 0; cc < Cfg::CC; ++cc) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const int n = nblk0 + cc * 64 + 8 * g + 2 * q;
+                if (n >= p.N) continue;
+                const float2 b = p.bias ? *reinterpret_cast<const float2*>(p.bias + n) : make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int m = mrow0 + 16 * s + 8 * h;
+                        if (m >= p.M) continue;
+                        const float2 a = acc[16 * (2 * cc + s) + 2 * g + h];
+                        *reinterpret_cast<__half2*>(out + static_cast<int64_t>(m) * p.ld_out + n) =
+                            __floats2half2_rn(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+                    }
+                }
             }
         }
     } else {
-        float* orow = reinterpret_cast<float*>(p.out) + static_cast<int64_t>(m) * p.ld_out;
-        const float* rrow = p.residual ? p.residual + static_cast<int64_t>(m) * p.ld_out : nullptr;
+        float* out = reinterpret_cast<float*>(p.out);
+        const bool add_bias = p.epi != B2Q_EPI_NONE && p.bias;
 #pragma unroll
-        for (int i = 0; i < Cfg::COLS / 2; i += 2) {
-            const int n = nbase + 2 * i;
-            if (n < p.N) {
-                float4 v = make_float4(acc[i].x, acc[i].y, acc[i + 1].x, acc[i + 1].y);
-                if (p.epi != B2Q_EPI_NONE && p.bias) {
-                    const float4 b = *reinterpret_cast<const float4*>(p.bias + n);
-                    v.x = __fadd_rn(v.x, b.x);
-                    v.y = __fadd_rn(v.y, b.y);
-                    v.z = __fadd_rn(v.z, b.z);
-                    v.w = __fadd_rn(v.w, b.w);
+        for (int cc = 0; cc < Cfg::CC; ++cc) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const int n = nblk0 + cc * 64 + 8 * g + 2 * q;
+                if (n >= p.N) continue;
+                const float2 b = add_bias ? *reinterpret_cast<const float2*>(p.bias + n) : make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int m = mrow0 + 16 * s + 8 * h;
+                        if (m >= p.M) continue;
+                        float2 v = acc[16 * (2 * cc + s) + 2 * g + h];
+                        if (add_bias) {
+                            v.x = __fadd_rn(v.x, b.x);
+                            v.y = __fadd_rn(v.y, b.y);
+                        }
+                        const int64_t off = static_cast<int64_t>(m) * p.ld_out + n;
+                        if (p.epi == B2Q_EPI_BIAS_RESIDUAL) {
+                            const float2 r = *reinterpret_cast<const float2*>(p.residual + off);
+                            v.x = __fadd_rn(v.x, r.x);
+                            v.y = __fadd_rn(v.y, r.y);
+                        }
+                        *reinterpret_cast<float2*>(out + off) = v;
+                    }
                 }
-                if (p.epi == B2Q_EPI_BIAS_RESIDUAL) {
-                    const float4 r = *reinterpret_cast<const float4*>(rrow + n);
-                    v.x = __fadd_rn(v.x, r.x);
-                    v.y = __fadd_rn(v.y, r.y);
-                    v.z = __fadd_rn(v.z, r.z);
-                    v.w = __fadd_rn(v.w, r.w);
-                }
-                *reinterpret_cast<float4*>(orow + n) = v;
             }
         }
     }
@@ -307,9 +336,9 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
     using Cfg = GemmCfg<kOps, kBN>;
     const int ew = warp - 4;
     const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
-    const int half = ew >> 2;                   // which BN/2 column half
-    const int row = quad * 32 + lane;           // row inside the tile
-    const int col0 = half * Cfg::COLS;
+    const int col0 = (ew >> 2) * Cfg::COLS;     // first column of this warp's half of the tile
+    const int q = lane & 3;
+    const int rloc = quad * 32 + (lane >> 2);   // tile row of (slab 0, h 0)
     const uint32_t taddr0 = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + col0;
     const int num_tiles = p.m_tiles * p.n_tiles;
     const int nst = (p.Kb + Cfg::KBS - 1) / Cfg::KBS;
@@ -317,37 +346,43 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
     Ring<Cfg::NBUF> acc_ring;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
         const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles;
-        const int m = mb * Cfg::BM + row;
-        const int nbase = nb * Cfg::BN + col0;
+        const int mrow0 = mb * Cfg::BM + rloc;
+        const int nblk0 = nb * Cfg::BN + col0;
         float2 acc[Cfg::COLS / 2];
 #pragma unroll
         for (int i = 0; i < Cfg::COLS / 2; ++i) acc[i] = make_float2(0.0f, 0.0f);
         uint32_t ra[32], rb[32];
-        if (!mbar_wait(&sm.tfull[acc_ring.idx], acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
+        if (!mbar_wait(bar_at(sm.tfull, acc_ring.idx), acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
             raise_error(p.err, sm.abort_flag, kDevTimeoutTmemFull);
             return false;
         }
         tc_fence_after();
-        tmem_ld_32x32b_x32(taddr0 + acc_ring.idx * Cfg::BN, ra);
+        tmem_ld_16x256b_x8(taddr0 + acc_ring.idx * Cfg::BN, ra);
         int kb = 0;
         for (int st = 0; st < nst; ++st) {
             const uint32_t s = st_ring.idx;
-            if (!mbar_wait(&sm.full[s], st_ring.phase, sm.abort_flag, p.timeout_ns)) {
+            if (!mbar_wait(bar_at(sm.full, s), st_ring.phase, sm.abort_flag, p.timeout_ns)) {
                 raise_error(p.err, sm.abort_flag, kDevTimeoutFull);
                 return false;
             }
-            const uint8_t* sbase = sm.base + s * Cfg::STAGE_BYTES;
-            const float* sdx = reinterpret_cast<const float*>(sbase + Cfg::A_BYTES + Cfg::B_BYTES) + row;
-            const float4* sdw =
-                reinterpret_cast<const float4*>(sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES) + col0 / 4;
+            const uint32_t sbase = sm.base + s * Cfg::STAGE_BYTES;
+            const uint32_t sdx = sbase + Cfg::A_BYTES + Cfg::B_BYTES + rloc * 4;             // dX[j][row]
+            const uint32_t sdw = sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES + (col0 + 2 * q) * 4;  // dW[j][col]
             const int nkb = min(Cfg::KBS, p.Kb - st * Cfg::KBS);
 #pragma unroll
             for (int j = 0; j < Cfg::KBS; ++j) {
                 if (j < nkb) {
-                    const float dx = sdx[j * Cfg::BM];
-                    const float2 dx2 = make_float2(dx, dx);
-                    const float4* w4 = sdw + j * (Cfg::BN / 4);
+                    float2 dx[2][2];
+#pragma unroll
+                    for (int sl = 0; sl < 2; ++sl)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float v = lds_f32(sdx + (j * Cfg::BM + 16 * sl + 8 * h) * 4);
+                            dx[sl][h] = make_float2(v, v);
+                        }
+                    const uint32_t w2 = sdw + j * Cfg::BN * 4;
                     const bool has_next = kb + 1 < p.Kb;
+                    float2 wv[8];
 #pragma unroll
                     for (int c = 0; c < Cfg::CH; ++c) {
                         uint32_t(&cur)[32] = (c & 1) ? rb : ra;
@@ -356,40 +391,53 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
                         if (c == Cfg::CH - 1) {
                             tc_fence_before();
                             __syncwarp();
-                            if (lane == 0) mbar_arrive(&sm.tempty[acc_ring.idx]);
+                            if (lane == 0) mbar_arrive(bar_at(sm.tempty, acc_ring.idx));
                             acc_ring.next();
                             if (has_next) {
-                                if (!mbar_wait(&sm.tfull[acc_ring.idx], acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
+                                if (!mbar_wait(bar_at(sm.tfull, acc_ring.idx), acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
                                     raise_error(p.err, sm.abort_flag, kDevTimeoutTmemFull);
                                     return false;
                                 }
                                 tc_fence_after();
-                                tmem_ld_32x32b_x32(taddr0 + acc_ring.idx * Cfg::BN, nxt);
+                                tmem_ld_16x256b_x8(taddr0 + acc_ring.idx * Cfg::BN, nxt);
                             }
                         } else {
-                            tmem_ld_32x32b_x32(taddr0 + acc_ring.idx * Cfg::BN + (c + 1) * 32, nxt);
+                            const int c1 = c + 1;
+                            tmem_ld_16x256b_x8(taddr0 + acc_ring.idx * Cfg::BN +
+                                                   (static_cast<uint32_t>((c1 & 1) * 16) << 16) + (c1 >> 1) * 64,
+                                               nxt);
                         }
                         if constexpr (kDump) {
-                            if (m < p.M) {
+                            const int sl = c & 1, cc = c >> 1;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int m = mrow0 + 16 * sl + 8 * h;
+                                if (m >= p.M) continue;
                                 int32_t* drow = p.dump + (static_cast<int64_t>(kb) * p.M + m) * p.N;
 #pragma unroll
-                                for (int i = 0; i < 32; ++i) {
-                                    const int n = nbase + c * 32 + i;
-                                    if (n < p.N) drow[n] = static_cast<int32_t>(carrier_to_float<kOps>(cur[i]));
+                                for (int g = 0; g < 8; ++g) {
+                                    const int n = nblk0 + cc * 64 + 8 * g + 2 * q;
+                                    if (n >= p.N) continue;
+                                    drow[n] = static_cast<int32_t>(carrier_to_float<kOps>(cur[4 * g + 2 * h]));
+                                    drow[n + 1] = static_cast<int32_t>(carrier_to_float<kOps>(cur[4 * g + 2 * h + 1]));
                                 }
                             }
                         } else {
-                            rescale_chunk<kOps>(acc + c * 16, cur, w4 + c * 8, dx2);
+                            if ((c & 1) == 0) {
+#pragma unroll
+                                for (int g = 0; g < 8; ++g) wv[g] = lds_v2_f32(w2 + ((c >> 1) * 64 + 8 * g) * 4);
+                            }
+                            rescale_chunk<kOps>(acc + 16 * c, cur, wv, dx[c & 1][0], dx[c & 1][1]);
                         }
                     }
                     ++kb;
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.empty[s]);
+            if (lane == 0) mbar_arrive(bar_at(sm.empty, s));
             st_ring.next();
         }
-        if constexpr (!kDump) store_tile<kOps, kBN>(p, acc, m, nbase);
+        if constexpr (!kDump) store_tile<kOps, kBN>(p, acc, mrow0, nblk0, q);
     }
     return true;
 }
@@ -402,13 +450,15 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     using Cfg = GemmCfg<kOps, kBN>;
     extern __shared__ uint8_t smem_raw[];
     Smem sm;
-    sm.base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sm.base + Cfg::STAGES * Cfg::STAGE_BYTES);
-    sm.full = bars;                          // [STAGES] TMA landed
-    sm.empty = bars + Cfg::STAGES;           // [STAGES] MMA + epilogue done with the stage
-    sm.tfull = bars + 2 * Cfg::STAGES;       // [NBUF]   accumulator ready
-    sm.tempty = sm.tfull + Cfg::NBUF;        // [NBUF]   accumulator drained
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm.tempty + Cfg::NBUF);
+    // the 128-byte swizzle needs 1024-byte aligned stages
+    uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* bars = base + Cfg::STAGES * Cfg::STAGE_BYTES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8 * (2 * Cfg::STAGES + 2 * Cfg::NBUF));
+    sm.base = smem_u32(base);
+    sm.full = smem_u32(bars);
+    sm.empty = sm.full + 8 * Cfg::STAGES;
+    sm.tfull = sm.empty + 8 * Cfg::STAGES;
+    sm.tempty = sm.tfull + 8 * Cfg::NBUF;
     sm.abort_flag = tmem_slot + 1;
 
     const int warp = threadIdx.x >> 5;
@@ -416,12 +466,12 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::STAGES; ++s) {
-            mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], 1 + Cfg::EPI_WARPS);
+            mbar_init(bar_at(sm.full, s), 1);
+            mbar_init(bar_at(sm.empty, s), 1 + Cfg::EPI_WARPS);
         }
         for (int b = 0; b < Cfg::NBUF; ++b) {
-            mbar_init(&sm.tfull[b], 1);
-            mbar_init(&sm.tempty[b], Cfg::EPI_WARPS);
+            mbar_init(bar_at(sm.tfull, b), 1);
+            mbar_init(bar_at(sm.tempty, b), Cfg::EPI_WARPS);
         }
         *sm.abort_flag = 0u;
         fence_barrier_init();
@@ -448,7 +498,7 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (uint32_t i = 0; i < n_drain; ++i) {
                 const uint32_t g = issued - 1 - i;
                 volatile uint32_t no_abort = 0;
-                mbar_wait(&sm.full[g % Cfg::STAGES], (g / Cfg::STAGES) & 1u, &no_abort, 100000000ull);
+                mbar_wait(bar_at(sm.full, g % Cfg::STAGES), (g / Cfg::STAGES) & 1u, &no_abort, 100000000ull);
             }
         } else if (warp == 1 && lane == 0) {
             uint32_t issued = 0;
@@ -457,7 +507,7 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (issued > 0) {
                 volatile uint32_t no_abort = 0;
                 const uint32_t g = issued - 1;
-                mbar_wait(&sm.tfull[g % Cfg::NBUF], (g / Cfg::NBUF) & 1u, &no_abort, 100000000ull);
+                mbar_wait(bar_at(sm.tfull, g % Cfg::NBUF), (g / Cfg::NBUF) & 1u, &no_abort, 100000000ull);
             }
         }
     } else {
