@@ -149,6 +149,7 @@ b2q_status b2q_weight_register(const void* q8_0, int64_t N, int64_t K, int64_t r
     w->N = N;
     w->K = K;
     w->Kb = Kb;
+    w->Nd = (N + 63) / 64 * 64;
     w->mode = ds->mode;
     w->device = ds->device;
     const int es = ops_elem_bytes(w->mode);
@@ -156,10 +157,13 @@ b2q_status b2q_weight_register(const void* q8_0, int64_t N, int64_t K, int64_t r
     void* staged = nullptr;
     b2q_status st = B2Q_OK;
     if (cudaMalloc(&w->q, static_cast<size_t>(N * K * es)) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void**>(&w->d), static_cast<size_t>(Kb * N * 4)) != cudaSuccess) {
+        cudaMalloc(reinterpret_cast<void**>(&w->d), static_cast<size_t>(Kb * w->Nd * 4)) != cudaSuccess) {
         st = set_error(B2Q_ERR_NOMEM, "cudaMalloc of weight planes failed");
         goto fail;
     }
+    // scale slots of columns N..Nd-1 stay zero: those columns are computed (as 0) but never stored
+    if ((st = cuda_check(cudaMemsetAsync(w->d, 0, static_cast<size_t>(Kb * w->Nd * 4), s), "weight scale clear")))
+        goto fail;
     if (src_is_host) {
         if (cudaMalloc(&staged, static_cast<size_t>(N * row_bytes)) != cudaSuccess) {
             st = set_error(B2Q_ERR_NOMEM, "cudaMalloc of weight staging failed");
@@ -170,7 +174,7 @@ b2q_status b2q_weight_register(const void* q8_0, int64_t N, int64_t K, int64_t r
             goto fail;
         src = staged;
     }
-    if ((st = cuda_check(launch_repack_q8_0(src, N, Kb, row_bytes, w->mode, w->q, w->d, s), "repack launch")))
+    if ((st = cuda_check(launch_repack_q8_0(src, N, Kb, row_bytes, w->Nd, w->mode, w->q, w->d, s), "repack launch")))
         goto fail;
     if (staged) {
         if ((st = cuda_check(cudaStreamSynchronize(s), "weight repack"))) goto fail;

@@ -47,8 +47,8 @@ struct GemmCfg {
     static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
     static constexpr int EPI_WARPS = 8;
     static constexpr int THREADS = 128 + EPI_WARPS * 32;   // 384: launch allocation 168 regs/thread
-    static constexpr int WG0_REGS = 56;                    // 128*56 + 256*224 = 384*168
-    static constexpr int EPI_REGS = 224;
+    static constexpr int WG0_REGS = 40;                    // 128*40 + 256*232 = 384*168
+    static constexpr int EPI_REGS = 232;
     static constexpr int COLS = BN / 2;                    // columns per epilogue thread
     static constexpr int CC = COLS / 64;                   // 64-column chunks per epilogue thread
     static constexpr int CH = 2 * CC;                      // 16x256b.x8 TMEM loads per K block (2 slabs)
@@ -93,15 +93,18 @@ __device__ __forceinline__ float carrier_to_float(uint32_t r) {
 
 // One 16x256b.x8 chunk: 2 rows (lane t/4 and t/4 + 8 of a 16-lane slab) x
 // 8 column pairs.  acc[2g + h] += ((float)S * dW) * dX for row h, pair g.
+// w4[i] holds the weight scales of pairs 2i (x, y) and 2i + 1 (z, w).
 template <int kOps>
-__device__ __forceinline__ void rescale_chunk(float2* acc, const uint32_t (&r)[32], const float2 (&w2)[8], float2 dx0,
+__device__ __forceinline__ void rescale_chunk(float2* acc, const uint32_t (&r)[32], const float4 (&w4)[4], float2 dx0,
                                               float2 dx1) {
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
+        const float4 wq = w4[g >> 1];
+        const float2 w = (g & 1) ? make_float2(wq.z, wq.w) : make_float2(wq.x, wq.y);
         const float2 f0 = make_float2(carrier_to_float<kOps>(r[4 * g + 0]), carrier_to_float<kOps>(r[4 * g + 1]));
         const float2 f1 = make_float2(carrier_to_float<kOps>(r[4 * g + 2]), carrier_to_float<kOps>(r[4 * g + 3]));
-        acc[2 * g] = __ffma2_rn(__fmul2_rn(f0, w2[g]), dx0, acc[2 * g]);
-        acc[2 * g + 1] = __ffma2_rn(__fmul2_rn(f1, w2[g]), dx1, acc[2 * g + 1]);
+        acc[2 * g] = __ffma2_rn(__fmul2_rn(f0, w), dx0, acc[2 * g]);
+        acc[2 * g + 1] = __ffma2_rn(__fmul2_rn(f1, w), dx1, acc[2 * g + 1]);
     }
 }
 
@@ -367,7 +370,8 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
             }
             const uint32_t sbase = sm.base + s * Cfg::STAGE_BYTES;
             const uint32_t sdx = sbase + Cfg::A_BYTES + Cfg::B_BYTES + rloc * 4;             // dX[j][row]
-            const uint32_t sdw = sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES + (col0 + 2 * q) * 4;  // dW[j][col]
+            // dW[j][slot]: this thread's 16-byte vectors sit at slots 16i + 4q of each 64-column chunk
+            const uint32_t sdw = sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES + (col0 + 4 * q) * 4;
             const int nkb = min(Cfg::KBS, p.Kb - st * Cfg::KBS);
 #pragma unroll
             for (int j = 0; j < Cfg::KBS; ++j) {
@@ -381,8 +385,12 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
                             dx[sl][h] = make_float2(v, v);
                         }
                     const uint32_t w2 = sdw + j * Cfg::BN * 4;
+                    float4 wv[Cfg::CC][4];
+#pragma unroll
+                    for (int cc = 0; cc < Cfg::CC; ++cc)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) wv[cc][i] = lds_v4_f32(w2 + (cc * 64 + 16 * i) * 4);
                     const bool has_next = kb + 1 < p.Kb;
-                    float2 wv[8];
 #pragma unroll
                     for (int c = 0; c < Cfg::CH; ++c) {
                         uint32_t(&cur)[32] = (c & 1) ? rb : ra;
@@ -423,11 +431,7 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
                                 }
                             }
                         } else {
-                            if ((c & 1) == 0) {
-#pragma unroll
-                                for (int g = 0; g < 8; ++g) wv[g] = lds_v2_f32(w2 + ((c >> 1) * 64 + 8 * g) * 4);
-                            }
-                            rescale_chunk<kOps>(acc + 16 * c, cur, wv, dx[c & 1][0], dx[c & 1][1]);
+                            rescale_chunk<kOps>(acc + 16 * c, cur, wv[c >> 1], dx[c & 1][0], dx[c & 1][1]);
                         }
                     }
                     ++kb;
@@ -601,8 +605,8 @@ bool make_weight_maps(b2q_weight* w) {
     const CUtensorMapDataType dt = w->mode == kOpsF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
     return make_tmap_2d(&w->tm_q256, dt, w->q, w->K, w->N, w->K * es, 128 / es, 256, true) &&
            make_tmap_2d(&w->tm_q128, dt, w->q, w->K, w->N, w->K * es, 128 / es, 128, true) &&
-           make_tmap_2d(&w->tm_d256, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->N, w->Kb, w->N * 4, 256, kbs, false) &&
-           make_tmap_2d(&w->tm_d128, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->N, w->Kb, w->N * 4, 128, kbs, false);
+           make_tmap_2d(&w->tm_d256, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 256, kbs, false) &&
+           make_tmap_2d(&w->tm_d128, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 128, kbs, false);
 }
 
 }  // namespace b2q

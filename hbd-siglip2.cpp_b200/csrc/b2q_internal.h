@@ -54,11 +54,22 @@ struct b2q_weight {
     int64_t N = 0, K = 0, Kb = 0;
     int mode = 0;
     int device = -1;
+    int64_t Nd = 0;        // scale row pitch: N rounded up to 64 columns
     void* q = nullptr;     // [N][K] int8 (or fp16 carriers)
-    float* d = nullptr;    // [Kb][N] fp32 (exact widening of the fp16 scales)
+    float* d = nullptr;    // [Kb][Nd] fp32 (exact widening of the fp16 scales), columns
+                           // permuted inside each 64-column group (scale_slot)
     CUtensorMap tm_q256, tm_q128;   // box 128 B x {256,128} rows, 128-byte swizzle
     CUtensorMap tm_d256, tm_d128;   // box {256,128} x (scales per stage)
 };
+
+// Position of column n inside its 64-column group of the weight-scale rows.
+// The GEMM epilogue thread with column pairs 8g + 2q + {0,1} (g < 8, q < 4)
+// of a 64-column chunk reads them as four 16-byte vectors: vector i holds
+// pairs g = 2i and 2i + 1, and the four q lanes read 64 contiguous bytes.
+__host__ __device__ inline int64_t scale_slot(int64_t n) {
+    const int64_t c = n & 63, g = c >> 3, q = (c >> 1) & 3, e = c & 1;
+    return (n & ~int64_t(63)) | (16 * (g >> 1) + 4 * q + 2 * (g & 1) + e);
+}
 
 #define B2Q_REQUIRE_STATE()                                                                 \
     b2q::DeviceState* ds = b2q::state();                                                    \
@@ -66,8 +77,8 @@ struct b2q_weight {
 
 namespace b2q {
 // kernels (launchers return cudaError_t of the launch)
-cudaError_t launch_repack_q8_0(const void* raw, int64_t N, int64_t Kb, int64_t row_bytes, int mode, void* q,
-                               float* d, cudaStream_t s);
+cudaError_t launch_repack_q8_0(const void* raw, int64_t N, int64_t Kb, int64_t row_bytes, int64_t Nd, int mode,
+                               void* q, float* d, cudaStream_t s);
 cudaError_t launch_quantize_q8_1(const float* x, int64_t M, int64_t K, int64_t ldx, void* act, int mode,
                                  cudaStream_t s);
 cudaError_t launch_ln_quant(const float* x, const float* w, const float* b, float eps, int64_t M, int64_t H,

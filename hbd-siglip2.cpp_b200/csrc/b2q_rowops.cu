@@ -37,13 +37,13 @@ ActLayout act_layout(int64_t M, int64_t K, int mode) {
 // raw: N rows of Kb blocks {fp16 d; int8 q[32]} (34 bytes, 2-byte aligned).
 template <int kOps>
 __global__ void repack_q8_0_kernel(const uint8_t* __restrict__ raw, int64_t N, int64_t Kb, int64_t row_bytes,
-                                   void* __restrict__ q, float* __restrict__ d) {
+                                   int64_t Nd, void* __restrict__ q, float* __restrict__ d) {
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;   // one block per thread
     if (idx >= N * Kb) return;
     const int64_t n = idx / Kb, kb = idx % Kb;
     const uint8_t* blk = raw + n * row_bytes + kb * 34;
     const uint16_t dh = static_cast<uint16_t>(blk[0]) | (static_cast<uint16_t>(blk[1]) << 8);
-    d[kb * N + n] = __half2float(__ushort_as_half(dh));
+    d[kb * Nd + scale_slot(n)] = __half2float(__ushort_as_half(dh));
     const int64_t K = Kb * 32;
     if constexpr (kOps == kOpsF16) {
         __half* out = static_cast<__half*>(q) + n * K + kb * 32;
@@ -54,15 +54,17 @@ __global__ void repack_q8_0_kernel(const uint8_t* __restrict__ raw, int64_t N, i
     }
 }
 
-cudaError_t launch_repack_q8_0(const void* raw, int64_t N, int64_t Kb, int64_t row_bytes, int mode, void* q,
-                               float* d, cudaStream_t s) {
+cudaError_t launch_repack_q8_0(const void* raw, int64_t N, int64_t Kb, int64_t row_bytes, int64_t Nd, int mode,
+                               void* q, float* d, cudaStream_t s) {
     const int64_t total = N * Kb;
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((total + threads - 1) / threads);
     if (mode == kOpsF16)
-        repack_q8_0_kernel<kOpsF16><<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(raw), N, Kb, row_bytes, q, d);
+        repack_q8_0_kernel<kOpsF16><<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(raw), N, Kb, row_bytes, Nd, q,
+                                                             d);
     else
-        repack_q8_0_kernel<kOpsI8><<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(raw), N, Kb, row_bytes, q, d);
+        repack_q8_0_kernel<kOpsI8><<<grid, threads, 0, s>>>(static_cast<const uint8_t*>(raw), N, Kb, row_bytes, Nd, q,
+                                                            d);
     count_launch();
     return cudaGetLastError();
 }
