@@ -162,6 +162,45 @@ def reference_arm(args):
     return 0
 
 
+def fc1_gemm(M, weights=None, reps=5):
+    """Time the fc1 Q8_0 GEMM (N=4304, K=1152) with the GELU->q8_1 epilogue
+    at M tokens; CUDA events on the launching stream.  -> (ms per launch, TOPS)"""
+    import torch
+    import b2q
+    from b2q import synth
+    cfg = synth.TowerConfig()
+    if weights is None:
+        rng = np.random.default_rng(0)
+        weights = synth.quantize_q8_0((rng.standard_normal((cfg.ffn, cfg.hidden)) * 0.02).astype(np.float32))
+    W = b2q.Weight(weights, cfg.ffn, cfg.hidden)
+    act = b2q.act_empty(M, cfg.hidden)
+    act_o = b2q.act_empty(M, cfg.ffn)
+    b2q.quantize_q8_1(torch.randn((M, cfg.hidden), device="cuda"), act, M, cfg.hidden)
+    bias = torch.zeros(cfg.ffn, device="cuda")
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    W.release()
+    return ms, 2.0 * M * cfg.ffn * cfg.hidden / (ms * 1e-3) / 1e12
+
+
+def profile_gemm(tokens):
+    import b2q
+    b2q.init(0)
+    ms, tops = fc1_gemm(tokens, reps=2)
+    b2q.check_device()
+    print(json.dumps({"kernel": "gemm_q8_kernel fc1", "tokens": tokens, "ms": ms, "tops": tops}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -170,9 +209,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--images", type=int, default=N_IMAGES)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-gemm", type=int, default=0, metavar="TOKENS",
+                    help="only run the fc1 GEMM (GELU->q8_1 epilogue) at this token count, for ncu captures")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.profile_gemm:
+        return profile_gemm(args.profile_gemm)
 
     import torch
     import torch.distributed as dist
@@ -275,25 +318,8 @@ def main():
 
     # roofline of the dominant kernel: fc1 GEMM (N=4304, K=1152) with the
     # GELU->q8_1 epilogue at this rank's token count, CUDA events on the stream
-    W = b2q.Weight(ck.tensors["v.blk.0.ffn_up.weight"], cfg.ffn, cfg.hidden)
     M = my_tokens
-    act = b2q.act_empty(M, cfg.hidden)
-    act_o = b2q.act_empty(M, cfg.ffn)
-    b2q.quantize_q8_1(torch.randn((M, cfg.hidden), device="cuda"), act, M, cfg.hidden)
-    bias = torch.zeros(cfg.ffn, device="cuda")
-    for _ in range(3):
-        b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
-    torch.cuda.synchronize()
-    reps = 5
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    gemm_ms = e0.elapsed_time(e1) / reps
-    gemm_tops = 2.0 * M * cfg.ffn * cfg.hidden / (gemm_ms * 1e-3) / 1e12
-    W.release()
+    gemm_ms, gemm_tops = fc1_gemm(M, weights=ck.tensors["v.blk.0.ffn_up.weight"])
 
     if rank == 0:
         bf16_peak, hbm_peak, peak_src = peaks()

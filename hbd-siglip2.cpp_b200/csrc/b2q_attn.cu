@@ -74,9 +74,13 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-    __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&h);
+// (a, b) = head + tail: head = fp16(a, b), tail = fp16 of the remainders.
+__device__ __forceinline__ void split_half2(float a, float b, uint32_t& head, uint32_t& tail) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 t = __floats2half2_rn(a - hf.x, b - hf.y);
+    head = *reinterpret_cast<const uint32_t*>(&h);
+    tail = *reinterpret_cast<const uint32_t*>(&t);
 }
 
 // Copy `rows` rows of 72 halves (9 x 16 B) starting at src (row stride ld
@@ -121,9 +125,9 @@ attention_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __rest
     cp_async_commit();
 
     // per-warp state: rows warp*16 + {lane/4, lane/4 + 8}
-    float o[10][4];
+    float o[9][4];   // output columns 0..71 as 9 n-tiles of 8
 #pragma unroll
-    for (int i = 0; i < 10; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    for (int i = 0; i < 9; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
     uint32_t qa[5][4];
 
@@ -201,26 +205,31 @@ attention_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __rest
             m_run[rr] = mx[rr];
         }
 #pragma unroll
-        for (int i = 0; i < 10; ++i) {
+        for (int i = 0; i < 9; ++i) {
             o[i][0] *= corr[0];
             o[i][1] *= corr[0];
             o[i][2] *= corr[1];
             o[i][3] *= corr[1];
         }
-        // O += P V: P (16 x 64) as 4 k-steps of A fragments built from the score tiles
+        // O += P V: P (16 x 64) as 4 k-steps of A fragments built from the
+        // score tiles.  P is split into an fp16 head and the fp16 rounding of
+        // its remainder (two products per fragment), so the probabilities
+        // keep ~22 bits instead of fp16's 11 and agree with the fp32 row
+        // sums; the padded output columns 72..79 are not computed.
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-            uint32_t pa[4];
-            pa[0] = pack_half2(s[2 * ks][0], s[2 * ks][1]);
-            pa[1] = pack_half2(s[2 * ks][2], s[2 * ks][3]);
-            pa[2] = pack_half2(s[2 * ks + 1][0], s[2 * ks + 1][1]);
-            pa[3] = pack_half2(s[2 * ks + 1][2], s[2 * ks + 1][3]);
+            uint32_t pa[4], pl[4];
+            split_half2(s[2 * ks][0], s[2 * ks][1], pa[0], pl[0]);
+            split_half2(s[2 * ks][2], s[2 * ks][3], pa[1], pl[1]);
+            split_half2(s[2 * ks + 1][0], s[2 * ks + 1][1], pa[2], pl[2]);
+            split_half2(s[2 * ks + 1][2], s[2 * ks + 1][3], pa[3], pl[3]);
 #pragma unroll
-            for (int nt = 0; nt < 10; ++nt) {
+            for (int nt = 0; nt < 9; ++nt) {
                 uint32_t vb[2];
                 const int r = ks * 16 + (lane & 15);
                 ldmatrix_x2_trans(vb, sV[buf] + r * kRowH + nt * 8);
                 mma_16816(o[nt], pa, vb);
+                mma_16816(o[nt], pl, vb);
             }
         }
         __syncthreads();

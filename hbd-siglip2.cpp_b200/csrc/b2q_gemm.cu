@@ -246,9 +246,7 @@ __device__ __forceinline__ void store_tile(const GemmParams& p, float2* acc, int
                         float amax = 0.0f;
 #pragma unroll
                         for (int gg = 0; gg < 4; ++gg) {
-                            const float2 a = acc[16 * (2 * cc + s) + 2 * (4 * bl + gg) + h];
-                            v[gg].x = gelu_tanh(__fadd_rn(a.x, b2[gg].x));
-                            v[gg].y = gelu_tanh(__fadd_rn(a.y, b2[gg].y));
+                            v[gg] = gelu2(__fadd2_rn(acc[16 * (2 * cc + s) + 2 * (4 * bl + gg) + h], b2[gg]));
                             amax = fmaxf(amax, fmaxf(fabsf(v[gg].x), fabsf(v[gg].y)));
                         }
                         // the block's 32 values of this row sit in the 4 lanes sharing t/4

@@ -15,8 +15,8 @@ namespace b2q {
 // e^r on |r| <= ln2/2, scaled by 2^n through the exponent field.
 __device__ __forceinline__ float own_expf(float x) {
     const float n = rintf(__fmul_rn(x, 1.44269504088896340736f));
-    float r = __fmaf_rn(-n, 0.693145751953125f, x);
-    r = __fmaf_rn(-n, 1.42860682030941723212e-6f, r);
+    float r = __fmaf_rn(n, -0.693145751953125f, x);
+    r = __fmaf_rn(n, -1.42860682030941723212e-6f, r);
     float p = 2.48015873015873015873e-5f;
     p = __fmaf_rn(p, r, 1.98412698412698412698e-4f);
     p = __fmaf_rn(p, r, 1.38888888888888888889e-3f);
@@ -30,43 +30,52 @@ __device__ __forceinline__ float own_expf(float x) {
     return __fmul_rn(p, __int_as_float((ni + 127) << 23));
 }
 
-// tanh: Maclaurin series to x^19 for |x| < 0.5625, 1 - 2/(e^{2|x|} + 1)
-// up to 9, +-1 beyond (within 2 ulp of the correctly rounded value).
-__device__ __forceinline__ float own_tanhf(float x) {
-    const float ax = fabsf(x);
-    if (ax < 0.5625f) {
-        const float x2 = __fmul_rn(x, x);
-        float q = -2.39129120018333196640e-04f;
-        q = __fmaf_rn(q, x2, 5.90027426369488239288e-04f);
-        q = __fmaf_rn(q, x2, -1.45583436824381351471e-03f);
-        q = __fmaf_rn(q, x2, 3.59212793409824371338e-03f);
-        q = __fmaf_rn(q, x2, -8.86323582381010055542e-03f);
-        q = __fmaf_rn(q, x2, 2.18694880604743957520e-02f);
-        q = __fmaf_rn(q, x2, -5.39682544767856597900e-02f);
-        q = __fmaf_rn(q, x2, 1.33333340287208557129e-01f);
-        q = __fmaf_rn(q, x2, -3.33333343267440795898e-01f);
-        const float x3 = __fmul_rn(x2, x);
-        return __fmaf_rn(q, x3, x);
-    }
-    float y;
-    if (ax < 9.0f) {
-        const float e = own_expf(__fmul_rn(2.0f, ax));
-        y = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(e, 1.0f)));
-    } else {
-        y = 1.0f;
-    }
-    return copysignf(y, x);
+// GELU, the tanh form of src/cuda/siglip2_megakernel.cu:276-280,
+// 0.5*x*(1+tanh(y)) with y = sqrt(2/pi)*x*(1+0.044715*x^2), evaluated as the
+// equal x / (1 + e^{-2y}): one exponential (own_expf, argument clamped to
+// +-80) and one division, branch-free.  The division a/b (b >= 1) is a
+// reciprocal seeded from the bit pattern (0x7EF311C7 - bits(b), the "magic
+// constant" method, relative error below 1/8), refined by three
+// Newton-Raphson steps y += y*(1 - b*y), and one Markstein correction of the
+// quotient q = q0 + y*(a - b*q0), q0 = a*y.  gelu2 does two elements with
+// packed f32x2 arithmetic; both perform, per element, exactly the operations
+// of the CPU checker's orc_gelu.
+__device__ __forceinline__ float2 own_div2(float2 a, float2 b) {
+    float2 y = make_float2(__int_as_float(0x7EF311C7 - __float_as_int(b.x)),
+                           __int_as_float(0x7EF311C7 - __float_as_int(b.y)));
+    const float2 nb = make_float2(-b.x, -b.y);
+    const float2 one = make_float2(1.0f, 1.0f);
+#pragma unroll
+    for (int it = 0; it < 3; ++it) y = __ffma2_rn(y, __ffma2_rn(nb, y, one), y);
+    const float2 q0 = __fmul2_rn(a, y);
+    return __ffma2_rn(__ffma2_rn(nb, q0, a), y, q0);
 }
 
-// GELU, tanh form of src/cuda/siglip2_megakernel.cu:276-280, evaluated left
-// to right: 0.5*x*(1+tanh(sqrt(2/pi)*x*(1+0.044715*x*x))).
-__device__ __forceinline__ float gelu_tanh(float x) {
-    const float x2 = __fmul_rn(x, x);
-    const float inner = __fadd_rn(1.0f, __fmul_rn(0.044715f, x2));
-    const float arg = __fmul_rn(__fmul_rn(0.79788456080286535587989211986876f, x), inner);
-    const float t = own_tanhf(arg);
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+__device__ __forceinline__ float2 gelu2(float2 x) {
+    const float2 x2 = __fmul2_rn(x, x);
+    const float2 inner = __ffma2_rn(make_float2(0.044715f, 0.044715f), x2, make_float2(1.0f, 1.0f));
+    const float c = -1.59576912160573071175978423973752f;   // -2*sqrt(2/pi)
+    float2 z = __fmul2_rn(__fmul2_rn(make_float2(c, c), x), inner);
+    z.x = fminf(fmaxf(z.x, -80.0f), 80.0f);
+    z.y = fminf(fmaxf(z.y, -80.0f), 80.0f);
+    // e^z, as own_expf
+    const float2 t = __fmul2_rn(z, make_float2(1.44269504088896340736f, 1.44269504088896340736f));
+    const float2 n = make_float2(rintf(t.x), rintf(t.y));
+    float2 r = __ffma2_rn(n, make_float2(-0.693145751953125f, -0.693145751953125f), z);
+    r = __ffma2_rn(n, make_float2(-1.42860682030941723212e-6f, -1.42860682030941723212e-6f), r);
+    const float kc[9] = {2.48015873015873015873e-5f, 1.98412698412698412698e-4f, 1.38888888888888888889e-3f,
+                         8.33333333333333333333e-3f, 4.16666666666666666667e-2f, 1.66666666666666666667e-1f,
+                         0.5f, 1.0f, 1.0f};
+    float2 p = make_float2(kc[0], kc[0]);
+#pragma unroll
+    for (int i = 1; i < 9; ++i) p = __ffma2_rn(p, r, make_float2(kc[i], kc[i]));
+    const float2 sc = make_float2(__int_as_float((static_cast<int32_t>(n.x) + 127) << 23),
+                                  __int_as_float((static_cast<int32_t>(n.y) + 127) << 23));
+    const float2 d = __fadd2_rn(make_float2(1.0f, 1.0f), __fmul2_rn(p, sc));
+    return own_div2(x, d);
 }
+
+__device__ __forceinline__ float gelu(float x) { return gelu2(make_float2(x, x)).x; }
 
 // q8_1 element rule (src/cuda/siglip2_custom_mmq.cu:63-81): given the block
 // absmax a, inv = a == 0 ? 0 : 127/a, q = rint(x*inv) clamped to [-128,127].

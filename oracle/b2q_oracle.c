@@ -51,26 +51,33 @@ uint16_t orc_fp32_to_fp16(float f) {
 }
 
 /* ------------------------------------------------------------------------ */
-/* exp / tanh / GELU                                                         */
+/* exp / reciprocal / GELU                                                   */
 /*                                                                           */
-/* The reference's GELU (src/cuda/siglip2_megakernel.cu:276-280) calls the   */
-/* platform tanhf.  CPU and GPU tanhf differ in the last bits, so this       */
-/* library uses its own tanh on both sides (same operations in the same      */
-/* order, every step an IEEE-exact +,*,fma,/): a Cody-Waite range-reduced    */
-/* exp (ln2 split into a 16-bit head and a tail) with the degree-8 Taylor    */
-/* polynomial of e^r on |r| <= ln2/2, and for |x| < 0.5625 the Maclaurin     */
-/* series of tanh to x^19.  Error vs. a correctly rounded tanh is tested to  */
-/* stay within 2 ulp (tests/test_oracle.py).                                 */
+/* The reference's GELU (src/cuda/siglip2_megakernel.cu:276-280) is the      */
+/* tanh form 0.5*x*(1+tanh(y)), y = sqrt(2/pi)*x*(1+0.044715*x^2), with the  */
+/* platform tanhf.  CPU and GPU math libraries differ in the last bits, so   */
+/* this library evaluates the same function its own way on both sides, with */
+/* the same operations in the same order (every step an IEEE-exact +,*,fma): */
+/* 0.5*(1+tanh(y)) = 1/(1+e^{-2y}), hence gelu(x) = x / (1 + e^{-2y}); one   */
+/* exponential and one division, no cancellation for negative x.             */
+/*   exp: Cody-Waite reduction x = n ln2 + r (ln2 split into a 16-bit head   */
+/*        and its tail), degree-8 Taylor polynomial of e^r on |r| <= ln2/2,  */
+/*        2^n through the exponent field.                                    */
+/*   a/b: reciprocal seed from the integer bit pattern (the "magic constant" */
+/*        method: 0x7EF311C7 - bits(b), relative error below 1/8), three     */
+/*        Newton-Raphson steps y += y*(1 - b*y), then one Markstein          */
+/*        correction q = q0 + y*(a - b*q0) of the quotient q0 = a*y.         */
+/* Error vs. the float64 tanh form is tested in tests/test_oracle.py.        */
 /* ------------------------------------------------------------------------ */
 #define ORC_LOG2E   1.44269504088896340736f
 #define ORC_LN2_HI  0.693145751953125f          /* 0x3F317200 */
 #define ORC_LN2_LO  1.42860682030941723212e-6f  /* ln2 - LN2_HI */
 
 float orc_expf(float x) {
-    /* valid for |x| <= 80 (callers stay far inside) */
+    /* valid for |x| <= 80 (callers clamp) */
     float n = rintf(x * ORC_LOG2E);
-    float r = fmaf(-n, ORC_LN2_HI, x);
-    r = fmaf(-n, ORC_LN2_LO, r);
+    float r = fmaf(n, -ORC_LN2_HI, x);
+    r = fmaf(n, -ORC_LN2_LO, r);
     float p = 2.48015873015873015873e-5f;            /* 1/8! */
     p = fmaf(p, r, 1.98412698412698412698e-4f);      /* 1/7! */
     p = fmaf(p, r, 1.38888888888888888889e-3f);      /* 1/6! */
@@ -87,52 +94,34 @@ float orc_expf(float x) {
     return p * s.f;
 }
 
-float orc_tanhf(float x) {
-    float ax = fabsf(x);
-    float y;
-    if (ax < 0.5625f) {
-        /* Maclaurin coefficients 2^2n (2^2n - 1) B_2n / (2n)! of x^(2n-1),
-         * n = 2..10, rounded to fp32 */
-        const float c1 = -3.33333343267440795898e-01f;   /* -1/3                      */
-        const float c2 =  1.33333340287208557129e-01f;   /*  2/15                     */
-        const float c3 = -5.39682544767856597900e-02f;   /* -17/315                   */
-        const float c4 =  2.18694880604743957520e-02f;   /*  62/2835                  */
-        const float c5 = -8.86323582381010055542e-03f;   /* -1382/155925              */
-        const float c6 =  3.59212793409824371338e-03f;   /*  21844/6081075            */
-        const float c7 = -1.45583436824381351471e-03f;   /* -929569/638512875         */
-        const float c8 =  5.90027426369488239288e-04f;   /*  6404582/10854718875      */
-        const float c9 = -2.39129120018333196640e-04f;   /* -443861162/1856156927625  */
-        float x2 = x * x;
-        float q = c9;
-        q = fmaf(q, x2, c8);
-        q = fmaf(q, x2, c7);
-        q = fmaf(q, x2, c6);
-        q = fmaf(q, x2, c5);
-        q = fmaf(q, x2, c4);
-        q = fmaf(q, x2, c3);
-        q = fmaf(q, x2, c2);
-        q = fmaf(q, x2, c1);
-        float x3 = x2 * x;
-        return fmaf(q, x3, x);
-    } else if (ax < 9.0f) {
-        float e = orc_expf(2.0f * ax);
-        y = 1.0f - 2.0f / (e + 1.0f);
-    } else {
-        y = 1.0f;
+float orc_div(float a, float b) {
+    /* b normal and positive (callers: b = 1 + e^z >= 1) */
+    union { float f; int32_t i; } u;
+    u.f = b;
+    u.i = 0x7EF311C7 - u.i;
+    float y = u.f;
+    for (int it = 0; it < 3; ++it) {
+        float e = fmaf(-b, y, 1.0f);
+        y = fmaf(y, e, y);
     }
-    return copysignf(y, x);
+    float q0 = a * y;
+    float r = fmaf(-b, q0, a);
+    return fmaf(r, y, q0);
 }
 
 float orc_gelu(float x) {
-    /* siglip2_megakernel.cu:276-280, evaluated left to right without
-     * contraction: 0.5*x*(1+tanh(c*x*(1+a*x*x))) */
-    const float GELU_COEF_A    = 0.044715f;
-    const float SQRT_2_OVER_PI = 0.79788456080286535587989211986876f;
-    float x2    = x * x;
-    float inner = 1.0f + GELU_COEF_A * x2;
-    float arg   = (SQRT_2_OVER_PI * x) * inner;
-    float t     = orc_tanhf(arg);
-    return (0.5f * x) * (1.0f + t);
+    const float GELU_COEF_A = 0.044715f;
+    const float M2_SQRT_2_OVER_PI = -1.59576912160573071175978423973752f;   /* -2*sqrt(2/pi) */
+    float x2 = x * x;
+    float inner = fmaf(GELU_COEF_A, x2, 1.0f);
+    float z = (M2_SQRT_2_OVER_PI * x) * inner;     /* -2y */
+    z = fminf(fmaxf(z, -80.0f), 80.0f);
+    float d = 1.0f + orc_expf(z);
+    return orc_div(x, d);
+}
+
+void orc_gelu_n(const float *x, int64_t n, float *y) {
+    for (int64_t i = 0; i < n; ++i) y[i] = orc_gelu(x[i]);
 }
 
 /* ------------------------------------------------------------------------ */

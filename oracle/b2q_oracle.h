@@ -24,8 +24,9 @@
  *   LayerNorm      per-row sums in the 32-lane x float4 order described at
  *                  orc_layernorm; inv_std = 1/sqrt(var+eps) correctly rounded
  *                                                            (siglip2_megakernel.cu:81-121)
- *   GELU           0.5*x*(1+tanh(sqrt(2/pi)*x*(1+0.044715*x*x))) with the
- *                  library's own tanh (orc_tanhf)            (siglip2_megakernel.cu:276-280)
+ *   GELU           the tanh form 0.5*x*(1+tanh(y)) evaluated as the equal
+ *                  x / (1 + e^{-2y}) with the library's own exp and division
+ *                  (orc_gelu)                                (siglip2_megakernel.cu:276-280)
  *   bias/residual  (mm + b) + r, two separately rounded adds (siglip2_megakernel.cu:287-300)
  */
 #ifndef B2Q_ORACLE_H
@@ -42,8 +43,9 @@ extern "C" {
 float    orc_fp16_to_fp32(uint16_t h);
 uint16_t orc_fp32_to_fp16(float f);
 float    orc_expf(float x);
-float    orc_tanhf(float x);
+float    orc_div(float a, float b);
 float    orc_gelu(float x);
+void     orc_gelu_n(const float *x, int64_t n, float *y);
 int      orc_num_threads(void);
 void     orc_set_num_threads(int n);
 

@@ -43,8 +43,9 @@ def _declare(L):
     L.orc_fp16_to_fp32.argtypes = [C.c_uint16]; L.orc_fp16_to_fp32.restype = C.c_float
     L.orc_fp32_to_fp16.argtypes = [C.c_float]; L.orc_fp32_to_fp16.restype = C.c_uint16
     L.orc_expf.argtypes = [C.c_float]; L.orc_expf.restype = C.c_float
-    L.orc_tanhf.argtypes = [C.c_float]; L.orc_tanhf.restype = C.c_float
+    L.orc_div.argtypes = [C.c_float, C.c_float]; L.orc_div.restype = C.c_float
     L.orc_gelu.argtypes = [C.c_float]; L.orc_gelu.restype = C.c_float
+    L.orc_gelu_n.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]; L.orc_gelu_n.restype = None
     L.orc_num_threads.restype = C.c_int
     L.orc_set_num_threads.argtypes = [C.c_int]
     L.orc_quantize_q8_0.argtypes = [P, I64, I64, I64, P]
@@ -73,13 +74,19 @@ def num_threads() -> int:
 
 
 # ---- scalar -----------------------------------------------------------------
-def tanhf(x: float) -> float:
-    return lib().orc_tanhf(float(x))
+def div(a: float, b: float) -> float:
+    return lib().orc_div(float(a), float(b))
+
+
+def gelu(x: float) -> float:
+    return lib().orc_gelu(float(x))
 
 
 def gelu_vec(x: np.ndarray) -> np.ndarray:
-    L = lib()
-    return np.array([L.orc_gelu(float(v)) for v in x.ravel()], np.float32).reshape(x.shape)
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().orc_gelu_n(_p(x), x.size, _p(y))
+    return y
 
 
 def expf(x: float) -> float:
