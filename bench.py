@@ -38,14 +38,43 @@ sys.path.insert(0, str(ROOT / "hbd-siglip2.cpp_b200"))
 METRIC = "Q8_0 vision images/s at 1/2/4/8 B200; MMQ GEMM int8 TOPS vs peak"
 N_IMAGES = 512
 PATCH_DIM = 768
-# DRAM bytes per token of one fc1 launch (dram__bytes_read + dram__bytes_write)
-# from the ncu capture summarised in profiles/gemm_fc1_launch_traffic.md, scaled
-# to the batch's token count (traffic grows in proportion to M).
-FC1_DRAM_BYTES_PER_TOKEN = None
+# DRAM bytes per token of one fc1 launch: dram__bytes_read + dram__bytes_write
+# = 171.15 + 548.74 MB from one ncu capture (one pass) of
+# `bench.py --profile-gemm 65536`, scaled to the batch's token count (the
+# traffic grows in proportion to M).
+FC1_DRAM_BYTES_PER_TOKEN = (171.15e6 + 548.74e6) / 65536
 
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
+
+
+def int8_peak_tops():
+    """Dense int8 tensor-core reference measured here: cuBLASLt int8 x int8 ->
+    int32 GEMM (torch._int_mm) at 8192^3, best of 10 after warm-up (a library
+    GEMM used as the yardstick, not part of the measured path)."""
+    import torch
+    try:
+        n = 8192
+        a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda")
+        b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device="cuda").t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        torch.cuda.empty_cache()
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    except RuntimeError as exc:      # no int8 GEMM in this torch build
+        log(f"int8 reference GEMM unavailable: {exc}")
+        return None
 
 
 def peaks():
@@ -111,12 +140,6 @@ class ClockSampler:
             pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": sorted(reasons)}
-
-
-def shard(grids, rank, world):
-    """Length-balanced deal: sort images by patch count, deal round-robin."""
-    order = sorted(range(len(grids)), key=lambda i: -grids[i][0] * grids[i][1])
-    return sorted(order[rank::world])
 
 
 def cpu_tower_sample(threads=None):
@@ -221,6 +244,7 @@ def main():
     import torch.distributed as dist
     import b2q
     from b2q import synth
+    from b2q.shard import gather_in_order, per_rank_capacity, shard_images
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -239,7 +263,7 @@ def main():
     log(f"[rank {rank}] weights ready in {time.time() - t0:.1f}s")
 
     grids = synth.naflex_grids(args.images, seed=0)
-    mine = shard(grids, rank, world)
+    mine = shard_images(grids, rank, world)
     my_grids = [grids[i] for i in mine]
     my_tokens = sum(h * w for h, w in my_grids)
     total_tokens = sum(h * w for h, w in grids)
@@ -251,23 +275,23 @@ def main():
         off += n
     dev = host.cuda()
     tower.reserve(my_tokens, len(my_grids))
-    per_rank = (args.images + world - 1) // world
+    per_rank = per_rank_capacity(args.images, world)
     emb = torch.zeros((per_rank, cfg.hidden), dtype=torch.float32, device="cuda")
-    gathered = torch.zeros((world * per_rank, cfg.hidden), dtype=torch.float32, device="cuda")
+    mine_dev = torch.tensor(mine, dtype=torch.int64, device="cuda")
     stream = torch.cuda.current_stream()
 
     def gather():
+        # pooled embeddings of all images, in the batch's order, on every rank
         if world > 1:
-            dist.all_gather_into_tensor(gathered, emb)
-        else:
-            gathered[:per_rank].copy_(emb)
+            return gather_in_order(emb[:len(mine)], mine_dev, args.images)
+        return emb[:len(mine)]
 
     def step_device():
         tower.encode(dev, my_grids, b2q.POOL_PROBE, out=emb)
         gather()
 
     out_host = np.empty((len(my_grids), cfg.hidden), np.float32)
-    gathered_host = torch.empty((world * per_rank, cfg.hidden), dtype=torch.float32, pin_memory=True)
+    gathered_host = torch.empty((args.images, cfg.hidden), dtype=torch.float32, pin_memory=True)
 
     def step_e2e():
         # public host-buffer entry point: pinned patches in, embeddings out
@@ -278,9 +302,9 @@ def main():
                                                    C.c_void_p(stream.cuda_stream)))
         if world > 1:
             emb[:len(my_grids)].copy_(torch.from_numpy(out_host), non_blocking=False)
-            dist.all_gather_into_tensor(gathered, emb)
+            allemb = gather_in_order(emb[:len(mine)], mine_dev, args.images)
             if rank == 0:
-                gathered_host.copy_(gathered)
+                gathered_host.copy_(allemb)
 
     def timed(fn, steps):
         if world > 1:
@@ -321,6 +345,7 @@ def main():
     M = my_tokens
     gemm_ms, gemm_tops = fc1_gemm(M, weights=ck.tensors["v.blk.0.ffn_up.weight"])
 
+    i8_peak = int8_peak_tops() if rank == 0 else None
     if rank == 0:
         bf16_peak, hbm_peak, peak_src = peaks()
         cpu = None
@@ -350,7 +375,9 @@ def main():
             "roofline": {"kernel": "gemm_q8_kernel (fc1, N=4304, K=1152, GELU->q8_1 epilogue)",
                          "bound": "tensor", "achieved": gemm_tops, "peak": bf16_peak / 1.0, "unit": "TFLOP/s",
                          "frac": gemm_tops / bf16_peak, "peak_source": f"bf16 dense, {peak_src}",
-                         "launch_ms": gemm_ms, "M": M, "traffic": traffic},
+                         "launch_ms": gemm_ms, "M": M, "traffic": traffic,
+                         "int8_peak_measured": i8_peak,
+                         "frac_int8": (gemm_tops / i8_peak) if i8_peak else None},
             "gemm_tops": gemm_tops,
             "gpu_launches": int(launches),
             "clocks": clocks,

@@ -211,3 +211,26 @@ def test_bad_arguments_return_status(mode):
     with pytest.raises(b2q.B2QError) as e:
         b2q.Weight(np.zeros((3, 34), np.uint8), 3, 32)
     assert e.value.status == b2q.ERR_SHAPE
+
+
+# ---------------------------------------------------------------- stored known-answer vectors
+def test_golden_vectors(mode):
+    """The CUDA path against tests/golden/gemm_small.npz (generated by
+    make_gemm_golden.py): q8_1 planes, int32 block sums and fp32 outputs."""
+    from pathlib import Path
+    z = np.load(Path(__file__).resolve().parent / "golden" / "gemm_small.npz")
+    for i, (M, N, K, Kp) in enumerate(z["cases"].tolist()):
+        W = b2q.Weight(z[f"wq{i}"], N, Kp)
+        act = b2q.act_empty(M, Kp)
+        b2q.quantize_q8_1(dev(z[f"x{i}"]), act, M, K)
+        q, d = b2q.act_planes(act, M, Kp)
+        np.testing.assert_array_equal(q.cpu().numpy(), z[f"qs{i}"])
+        np.testing.assert_array_equal(d.cpu().numpy(), z[f"d{i}"])
+        bs = torch.zeros((Kp // 32, M, N), dtype=torch.int32, device="cuda")
+        b2q.block_sums(W, act, M, bs)
+        np.testing.assert_array_equal(bs.cpu().numpy(), z[f"s{i}"].transpose(2, 0, 1))
+        y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        b2q.mul_mat(W, act, M, y)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(y.cpu().numpy(), z[f"y{i}"])
+        W.release()

@@ -130,6 +130,22 @@ def test_division_and_gelu_accuracy(oracle):
     assert oracle.gelu(0.0) == 0.0 and oracle.gelu(1e4) == 1e4
 
 
+def test_oracle_reproduces_gemm_golden_vectors(oracle):
+    """tests/golden/gemm_small.npz (make_gemm_golden.py) pins the oracle's
+    q8_1 planes, int32 block sums and fp32 outputs; the GPU suite checks the
+    CUDA path against the same stored vectors."""
+    from pathlib import Path
+    z = np.load(Path(__file__).resolve().parent / "golden" / "gemm_small.npz")
+    for i, (M, N, K, Kp) in enumerate(z["cases"].tolist()):
+        qs, d = oracle.quantize_q8_1(z[f"x{i}"], Kp)
+        np.testing.assert_array_equal(qs, z[f"qs{i}"])
+        np.testing.assert_array_equal(d, z[f"d{i}"])
+        y, s = oracle.gemm_q8(z[f"wq{i}"], N, Kp, qs, d, block_sums=True)
+        np.testing.assert_array_equal(s, z[f"s{i}"])
+        np.testing.assert_array_equal(y, z[f"y{i}"])
+    assert z["qs0"].min() == 0 and z["qs0"].max() == 0 and z["d0"].max() == 0.0   # all-zero block
+
+
 def test_layernorm_matches_float64(oracle):
     rng = np.random.default_rng(4)
     x = rng.standard_normal((9, 1152)).astype(np.float32) * 3 + 1
