@@ -28,6 +28,8 @@ EXPORTS = [
     "b2q_attention_scratch_bytes", "b2q_attention",
     "b2q_vision_create", "b2q_vision_destroy", "b2q_vision_set_tensor", "b2q_vision_reserve",
     "b2q_vision_encode", "b2q_vision_encode_host",
+    "b2q_text_create", "b2q_text_destroy", "b2q_text_set_tensor", "b2q_text_reserve", "b2q_text_encode",
+    "b2q_text_encode_host", "b2q_score_scratch_bytes", "b2q_score",
 ]
 
 
@@ -40,6 +42,11 @@ class B2QError(RuntimeError):
 class VisionConfig(C.Structure):
     _fields_ = [("hidden", C.c_int32), ("ffn", C.c_int32), ("n_head", C.c_int32), ("n_layer", C.c_int32),
                 ("patch_dim", C.c_int32), ("pos_side", C.c_int32), ("eps", C.c_float)]
+
+
+class TextConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("ffn", C.c_int32), ("n_head", C.c_int32), ("n_layer", C.c_int32),
+                ("vocab", C.c_int32), ("n_pos", C.c_int32), ("eps", C.c_float)]
 
 
 POOL_MEAN, POOL_PROBE = 0, 1
@@ -90,6 +97,15 @@ def lib():
         L.b2q_vision_reserve.argtypes = [P, I64, C.c_int32]
         L.b2q_vision_encode.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
         L.b2q_vision_encode_host.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
+        L.b2q_text_create.argtypes = [C.POINTER(TextConfig), C.POINTER(P)]
+        L.b2q_text_destroy.argtypes = [P]
+        L.b2q_text_set_tensor.argtypes = [P, C.c_char_p, C.c_int32, P, I64, I64, P]
+        L.b2q_text_reserve.argtypes = [P, C.c_int32]
+        L.b2q_text_encode.argtypes = [P, P, C.c_int32, P, P]
+        L.b2q_text_encode_host.argtypes = [P, P, C.c_int32, P, P]
+        L.b2q_score_scratch_bytes.argtypes = [C.c_int32, C.c_int32, C.c_int32]
+        L.b2q_score_scratch_bytes.restype = C.c_size_t
+        L.b2q_score.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int32, C.c_float, C.c_float, P, P, P, P]
         for name in EXPORTS:
             fn = getattr(L, name)
             if name not in ("b2q_last_error", "b2q_abi_version", "b2q_act_bytes", "b2q_attention_scratch_bytes",
@@ -306,3 +322,75 @@ class VisionTower:
             self.close()
         except Exception:
             pass
+
+
+class TextTower:
+    """Batched SigLIP2 text tower (the C++ driver behind b2q_text_*)."""
+
+    def __init__(self, cfg):
+        self.cfg = cfg
+        c = TextConfig(cfg.hidden, cfg.ffn, cfg.n_head, cfg.n_layer, cfg.vocab, cfg.n_pos, cfg.eps)
+        h = C.c_void_p()
+        check(lib().b2q_text_create(C.byref(c), C.byref(h)))
+        self.handle = h
+
+    def set_tensor(self, name: str, arr: np.ndarray, q8_shape=None, stream=None):
+        arr = np.ascontiguousarray(arr)
+        if q8_shape is not None:
+            n, _, kp = q8_shape
+            check(lib().b2q_text_set_tensor(self.handle, name.encode(), GGML_Q8_0, arr.ctypes.data, kp, n,
+                                            _stream(stream)))
+        else:
+            a = np.ascontiguousarray(arr, np.float32)
+            ne0 = a.shape[-1]
+            check(lib().b2q_text_set_tensor(self.handle, name.encode(), GGML_F32, a.ctypes.data, ne0, a.size // ne0,
+                                            _stream(stream)))
+
+    def load(self, ck, stream=None):
+        for name, arr in ck.tensors.items():
+            if name.startswith("t."):
+                self.set_tensor(name, arr, ck.q8_shapes.get(name), stream)
+
+    def reserve(self, max_prompts: int):
+        check(lib().b2q_text_reserve(self.handle, max_prompts))
+
+    def encode(self, ids, out=None, stream=None):
+        """ids: torch CUDA int32 [n_prompts][n_pos]."""
+        import torch
+        n = ids.shape[0]
+        if out is None:
+            out = torch.empty((n, self.cfg.hidden), dtype=torch.float32, device="cuda")
+        check(lib().b2q_text_encode(self.handle, _ptr(ids), n, _ptr(out), _stream(stream)))
+        return out
+
+    def encode_host(self, ids: np.ndarray, stream=None) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.empty((ids.shape[0], self.cfg.hidden), np.float32)
+        check(lib().b2q_text_encode_host(self.handle, ids.ctypes.data, ids.shape[0], out.ctypes.data,
+                                         _stream(stream)))
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().b2q_text_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def score(img, txt, logit_scale: float, logit_bias: float, logits=True, probs=True, stream=None):
+    """Image-text sigmoid scores on the device (b2q_score); img [I][H], txt [J][H]
+    torch CUDA fp32.  Returns (logits, probs), either None if not requested."""
+    import torch
+    I, H = img.shape
+    J = txt.shape[0]
+    scratch = torch.empty(int(lib().b2q_score_scratch_bytes(I, J, H)), dtype=torch.uint8, device="cuda")
+    lg = torch.empty((I, J), dtype=torch.float32, device="cuda") if logits else None
+    pr = torch.empty((I, J), dtype=torch.float32, device="cuda") if probs else None
+    check(lib().b2q_score(_ptr(img), I, _ptr(txt), J, H, float(logit_scale), float(logit_bias), _ptr(lg), _ptr(pr),
+                          _ptr(scratch), _stream(stream)))
+    return lg, pr

@@ -349,10 +349,10 @@ int attn_build_tiles(const int* q_off, const int* q_len, const int* k_off, const
 
 cudaError_t launch_attention(const __half* q, int64_t ldq, const __half* k, int64_t ldk, const __half* v,
                              int64_t ldv, const void* tiles_dev, int n_tiles, int n_head, float* out, int64_t ldo,
-                             cudaStream_t s) {
+                             cudaStream_t s, bool force_exact) {
     if (n_tiles <= 0) return cudaSuccess;
     DeviceState* ds = state();
-    if (ds && ds->attn_exact) {
+    if (force_exact || (ds && ds->attn_exact)) {
         const float scale = 1.0f / sqrtf(static_cast<float>(kDH));
         dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_head));
         attention_exact_kernel<<<grid, kExactThreads, 0, s>>>(q, ldq, k, ldk, v, ldv,

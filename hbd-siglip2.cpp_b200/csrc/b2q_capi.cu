@@ -130,6 +130,8 @@ b2q_status b2q_check_device(void* stream, uint32_t* code_out) {
     if ((st = cuda_check(cudaMemcpy(&code, ds->err, 4, cudaMemcpyDeviceToHost), "read device error word"))) return st;
     if (code) cudaMemset(ds->err, 0, 4);
     if (code_out) *code_out = code;
+    if (code == 5u)   // kDevBadTokenId
+        return set_error(B2Q_ERR_DEVICE, "a token id outside the vocabulary (code 5)");
     if (code) return set_error(B2Q_ERR_DEVICE, "a kernel's bounded wait expired (code " + std::to_string(code) + ")");
     return B2Q_OK;
 }

@@ -89,7 +89,7 @@ int attn_build_tiles(const int* q_off, const int* q_len, const int* k_off, const
 size_t attn_tiles_bytes(int n_tiles);
 cudaError_t launch_attention(const __half* q, int64_t ldq, const __half* k, int64_t ldk, const __half* v,
                              int64_t ldv, const void* tiles_dev, int n_tiles, int n_head, float* out, int64_t ldo,
-                             cudaStream_t s);
+                             cudaStream_t s, bool force_exact = false);
 
 struct GemmArgs {
     const b2q_weight* w;

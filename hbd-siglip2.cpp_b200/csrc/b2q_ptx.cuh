@@ -19,6 +19,7 @@ enum : uint32_t {
     kDevTimeoutEmpty = 2,     // consumer never released a stage
     kDevTimeoutTmemFull = 3,  // MMA result never committed
     kDevTimeoutTmemEmpty = 4, // epilogue never released an accumulator
+    kDevBadTokenId = 5,       // a token id outside the vocabulary (replaced by 0)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -1,0 +1,297 @@
+// b2q_text.cu — SigLIP2 text tower driver and image-text scoring.
+//
+// Text: counterpart of TextEncoder::encode_batch (src/siglip2_text.cpp:741-932)
+// over the same Q8_0 hot path as the vision tower.  n_prompts prompts of
+// n_pos token ids are packed into one token stream; each prompt is its own
+// attention sequence (no mask: every prompt fills all n_pos positions, as the
+// reference's server pads them, src/siglip2_server.cpp:381-431), always with
+// the fixed-order fp32 attention kernel:
+//   x[t] = dequant(token_embd row ids[t]) + position_embd[t % n_pos]
+//                                          (get_rows + add, siglip2_text.cpp:837-847)
+//   27 pre-LN blocks                       (the vision block sequence)
+//   final LN of each prompt's last token, head GEMM + bias
+//                                          (siglip2_text.cpp:849-865)
+// Scoring: counterpart of score_image_text (src/siglip2_score.cpp:90-134):
+// rows L2-normalised in double with +1e-12, logit = dot * e^{logit_scale} +
+// logit_bias with the dot in double, sigmoid.  exp and the sigmoid's division
+// use the library's own functions (b2q_numerics.cuh) so the CPU checker
+// reproduces the probabilities bit for bit.
+#include "b2q_numerics.cuh"
+#include "b2q_ptx.cuh"
+#include "b2q_tower.h"
+
+#include <cmath>
+#include <string>
+#include <vector>
+
+namespace b2q {
+namespace {
+
+// x[t][:] = dequant(table row ids[t]) + pos[t % n_pos][:]; one CTA per token,
+// one thread per 32-element block (H/32 = 36 threads active).
+__global__ void embed_tokens_kernel(const uint8_t* __restrict__ table, int vocab, int H, const int32_t* __restrict__ ids,
+                                    const float* __restrict__ pos, int n_pos, float* __restrict__ x,
+                                    uint32_t* __restrict__ err) {
+    const int t = blockIdx.x;
+    int id = ids[t];
+    if (id < 0 || id >= vocab) {
+        if (threadIdx.x == 0) atomicCAS(err, 0u, kDevBadTokenId);
+        id = 0;
+    }
+    const int Kb = H / 32;
+    const uint8_t* row = table + static_cast<int64_t>(id) * Kb * 34;
+    const float* prow = pos + static_cast<int64_t>(t % n_pos) * H;
+    float* xrow = x + static_cast<int64_t>(t) * H;
+    for (int kb = threadIdx.x; kb < Kb; kb += blockDim.x) {
+        const uint8_t* blk = row + kb * 34;
+        const float d = __half2float(__ushort_as_half(static_cast<uint16_t>(blk[0] | (blk[1] << 8))));
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
+            const float e = __fmul_rn(static_cast<float>(static_cast<int8_t>(blk[2 + j])), d);
+            xrow[kb * 32 + j] = __fadd_rn(e, prow[kb * 32 + j]);
+        }
+    }
+}
+
+// pooled[p][:] = x[p * n_pos + n_pos - 1][:]
+__global__ void last_token_kernel(const float* __restrict__ x, int H, int n_pos, float* __restrict__ pooled) {
+    const int p = blockIdx.x;
+    const float4* src = reinterpret_cast<const float4*>(x + (static_cast<int64_t>(p) * n_pos + n_pos - 1) * H);
+    float4* dst = reinterpret_cast<float4*>(pooled + static_cast<int64_t>(p) * H);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+// In-place row L2 normalisation, one thread per row, sequential double sum in
+// column order (l2_normalize_rows, src/siglip2_score.cpp:77-86).
+__global__ void l2_normalize_kernel(const float* __restrict__ in, float* __restrict__ out, int rows, int H) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    const float* x = in + static_cast<int64_t>(r) * H;
+    float* y = out + static_cast<int64_t>(r) * H;
+    double sumsq = 0.0;
+    for (int c = 0; c < H; ++c) {
+        const double v = x[c];
+        sumsq = __dadd_rn(sumsq, __dmul_rn(v, v));
+    }
+    const float inv = static_cast<float>(__ddiv_rn(1.0, __dadd_rn(__dsqrt_rn(sumsq), 1e-12)));
+    for (int c = 0; c < H; ++c) y[c] = __fmul_rn(x[c], inv);
+}
+
+// logits[i][j] = (float)(dot(a_i, b_j) * (double)scale + (double)bias), the
+// dot accumulated in double over ascending columns; probs = sigmoid(logits)
+// in the numerically stable split form.  16 x 16 outputs per CTA, columns
+// staged through shared memory in chunks of 32.
+__global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ a, int I, const float* __restrict__ b,
+                                                    int J, int H, float logit_scale, float bias,
+                                                    float* __restrict__ logits, float* __restrict__ probs) {
+    __shared__ float sa[16][33], sb[16][33];
+    const int ti = threadIdx.y, tj = threadIdx.x;
+    const int i = blockIdx.y * 16 + ti, j = blockIdx.x * 16 + tj;
+    double dot = 0.0;
+    for (int c0 = 0; c0 < H; c0 += 32) {
+        for (int e = threadIdx.y * 16 + threadIdx.x; e < 16 * 32; e += 256) {
+            const int r = e / 32, c = e % 32;
+            const int ia = blockIdx.y * 16 + r, jb = blockIdx.x * 16 + r;
+            sa[r][c] = (ia < I && c0 + c < H) ? a[static_cast<int64_t>(ia) * H + c0 + c] : 0.0f;
+            sb[r][c] = (jb < J && c0 + c < H) ? b[static_cast<int64_t>(jb) * H + c0 + c] : 0.0f;
+        }
+        __syncthreads();
+        const int n = H - c0 < 32 ? H - c0 : 32;
+        for (int c = 0; c < n; ++c)
+            dot = __dadd_rn(dot, __dmul_rn(static_cast<double>(sa[ti][c]), static_cast<double>(sb[tj][c])));
+        __syncthreads();
+    }
+    if (i >= I || j >= J) return;
+    const float scale = own_expf(logit_scale);
+    const float logit = __double2float_rn(__dadd_rn(__dmul_rn(dot, static_cast<double>(scale)),
+                                                    static_cast<double>(bias)));
+    const int64_t o = static_cast<int64_t>(i) * J + j;
+    if (logits) logits[o] = logit;
+    if (probs) {
+        float p;
+        if (logit >= 0.0f) {
+            const float e = own_expf(logit < 80.0f ? -logit : -80.0f);
+            p = own_div2(make_float2(1.0f, 1.0f), make_float2(__fadd_rn(1.0f, e), 1.0f)).x;
+        } else {
+            const float e = own_expf(logit > -80.0f ? logit : -80.0f);
+            p = own_div2(make_float2(e, e), make_float2(__fadd_rn(1.0f, e), 1.0f)).x;
+        }
+        probs[o] = p;
+    }
+}
+
+}  // namespace
+}  // namespace b2q
+
+using namespace b2q;
+
+struct b2q_text {
+    b2q_text_config cfg{};
+    int ffn_pad = 0;
+    TensorSet ts;
+    int32_t cap_prompts = 0;
+    DevBuf x, qkv16, attn, act_h, act_f, tiles, pooled, ids_in, out_dev;
+    std::vector<uint8_t> host_tiles;
+    int n_tiles_for = -1, n_tiles = 0;   // tile table cached for this many prompts
+};
+
+namespace {
+
+b2q_status check_text(const b2q_text* t) {
+    if (!t->ts.raw("t.token_embd.weight") || !t->ts.f("t.position_embd.weight") || !t->ts.f("t.final_ln.weight") ||
+        !t->ts.f("t.final_ln.bias") || !t->ts.w("t.head.weight") || !t->ts.f("t.head.bias"))
+        return set_error(B2Q_ERR_INVALID, "text tower: embedding / final-LN / head tensors missing");
+    return check_blocks(t->ts, "t.", t->cfg.n_layer);
+}
+
+}  // namespace
+
+extern "C" {
+
+b2q_status b2q_text_create(const b2q_text_config* cfg, b2q_text** out) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!cfg || !out) return set_error(B2Q_ERR_INVALID, "null pointer");
+    if (cfg->hidden != cfg->n_head * 72 || cfg->hidden % 128 || cfg->hidden / 128 != 9 || cfg->ffn <= 0 ||
+        cfg->n_layer <= 0 || cfg->vocab <= 0 || cfg->n_pos <= 0)
+        return set_error(B2Q_ERR_SHAPE, "text config: needs hidden 1152 = 16 heads x 72 and positive sizes");
+    b2q_text* t = new b2q_text();
+    t->cfg = *cfg;
+    t->ffn_pad = static_cast<int>(round_up(cfg->ffn, 32));
+    *out = t;
+    return B2Q_OK;
+}
+
+b2q_status b2q_text_destroy(b2q_text* t) {
+    delete t;
+    return B2Q_OK;
+}
+
+b2q_status b2q_text_set_tensor(b2q_text* t, const char* name, int32_t ggml_type, const void* host_data, int64_t ne0,
+                               int64_t ne1, void* stream) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!t || !name || !host_data) return set_error(B2Q_ERR_INVALID, "null pointer");
+    const std::string n(name);
+    const bool table = n == "t.token_embd.weight";
+    if (table && (ggml_type != 8 || ne0 != t->cfg.hidden || ne1 != t->cfg.vocab))
+        return set_error(B2Q_ERR_SHAPE, "t.token_embd.weight must be Q8_0 [vocab][hidden]");
+    return t->ts.put(n, ggml_type, host_data, ne0, ne1, table, static_cast<cudaStream_t>(stream));
+}
+
+b2q_status b2q_text_reserve(b2q_text* t, int32_t max_prompts) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!t || max_prompts <= 0) return set_error(B2Q_ERR_INVALID, "bad reserve arguments");
+    const int64_t P = t->cfg.n_pos, H = t->cfg.hidden, T = static_cast<int64_t>(max_prompts) * P;
+    const int tiles = max_prompts * static_cast<int>((P + 63) / 64);
+    B2Q_TRY(cuda_check(t->x.ensure(T * H * 4), "cudaMalloc(x)"));
+    B2Q_TRY(cuda_check(t->qkv16.ensure(T * 3 * H * 2), "cudaMalloc(qkv)"));
+    B2Q_TRY(cuda_check(t->attn.ensure(T * H * 4), "cudaMalloc(attn)"));
+    B2Q_TRY(cuda_check(t->act_h.ensure(b2q_act_bytes(T, H)), "cudaMalloc(act_h)"));
+    B2Q_TRY(cuda_check(t->act_f.ensure(b2q_act_bytes(T, t->ffn_pad)), "cudaMalloc(act_f)"));
+    B2Q_TRY(cuda_check(t->tiles.ensure(attn_tiles_bytes(tiles)), "cudaMalloc(tiles)"));
+    B2Q_TRY(cuda_check(t->pooled.ensure(static_cast<size_t>(max_prompts) * H * 4), "cudaMalloc(pooled)"));
+    B2Q_TRY(cuda_check(t->ids_in.ensure(static_cast<size_t>(T) * 4), "cudaMalloc(ids)"));
+    B2Q_TRY(cuda_check(t->out_dev.ensure(static_cast<size_t>(max_prompts) * H * 4), "cudaMalloc(out)"));
+    t->host_tiles.resize(attn_tiles_bytes(tiles));
+    t->cap_prompts = max_prompts;
+    t->n_tiles_for = -1;
+    return B2Q_OK;
+}
+
+b2q_status b2q_text_encode(b2q_text* t, const int32_t* ids, int32_t n_prompts, float* out, void* stream) {
+    B2Q_REQUIRE_STATE();
+    if (!t || !ids || !out) return set_error(B2Q_ERR_INVALID, "null pointer");
+    if (n_prompts <= 0) return set_error(B2Q_ERR_INVALID, "n_prompts must be positive");
+    B2Q_TRY(check_text(t));
+    if (n_prompts > t->cap_prompts) B2Q_TRY(b2q_text_reserve(t, n_prompts));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const b2q_text_config& c = t->cfg;
+    const int64_t H = c.hidden, P = c.n_pos, T = static_cast<int64_t>(n_prompts) * P;
+
+    if (t->n_tiles_for != n_prompts) {
+        std::vector<int> off(n_prompts), len(n_prompts, static_cast<int>(P));
+        for (int p = 0; p < n_prompts; ++p) off[p] = static_cast<int>(p * P);
+        const int n = attn_build_tiles(off.data(), len.data(), off.data(), len.data(), off.data(), n_prompts,
+                                       t->host_tiles.data(),
+                                       static_cast<int>(t->host_tiles.size() / attn_tiles_bytes(1)));
+        if (n < 0) return set_error(B2Q_ERR_SHAPE, "attention tile table overflow");
+        B2Q_TRY(cuda_check(cudaMemcpyAsync(t->tiles.p, t->host_tiles.data(), attn_tiles_bytes(n),
+                                           cudaMemcpyHostToDevice, s),
+                           "tile table upload"));
+        B2Q_TRY(cuda_check(cudaStreamSynchronize(s), "tile table upload"));
+        t->n_tiles = n;
+        t->n_tiles_for = n_prompts;
+    }
+
+    float* x = t->x.as<float>();
+    embed_tokens_kernel<<<static_cast<unsigned>(T), 64, 0, s>>>(t->ts.raw("t.token_embd.weight"), c.vocab,
+                                                                 static_cast<int>(H), ids,
+                                                                 t->ts.f("t.position_embd.weight"),
+                                                                 static_cast<int>(P), x, ds->err);
+    count_launch();
+    B2Q_TRY(cuda_check(cudaGetLastError(), "token embedding launch"));
+
+    // attention in the fixed fp32 order: a text embedding is one token's row,
+    // so unlike the vision heads nothing averages out the q8_1 rounding
+    // decisions a non-reproducible attention would move; at n_pos = 64 the
+    // exact kernel costs little.  Text embeddings are thereby bit-identical
+    // to the CPU checker.
+    B2Q_TRY(run_encoder_blocks(t->ts, "t.", c.n_layer, c.n_head, c.eps, T, H, x, t->qkv16.as<__half>(),
+                               t->attn.as<float>(), t->act_h.p, t->act_f.p, t->tiles.p, t->n_tiles, true, s));
+
+    // final LN is per row: apply it to the pooled (last) rows only
+    float* pooled = t->pooled.as<float>();
+    last_token_kernel<<<static_cast<unsigned>(n_prompts), 96, 0, s>>>(x, static_cast<int>(H), static_cast<int>(P),
+                                                                      pooled);
+    count_launch();
+    B2Q_TRY(cuda_check(cudaGetLastError(), "pool launch"));
+    B2Q_TRY(b2q_ln_quantize_q8_1(pooled, t->ts.f("t.final_ln.weight"), t->ts.f("t.final_ln.bias"), c.eps, n_prompts,
+                                 H, t->act_h.p, nullptr, s));
+    return gemm(t->ts.w("t.head.weight"), t->act_h.p, n_prompts, out, B2Q_EPI_BIAS, t->ts.f("t.head.bias"), nullptr,
+                nullptr, 0, s);
+}
+
+b2q_status b2q_text_encode_host(b2q_text* t, const int32_t* ids_host, int32_t n_prompts, float* out_host,
+                                void* stream) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!t || !ids_host || !out_host) return set_error(B2Q_ERR_INVALID, "null pointer");
+    if (n_prompts <= 0) return set_error(B2Q_ERR_INVALID, "n_prompts must be positive");
+    if (n_prompts > t->cap_prompts) B2Q_TRY(b2q_text_reserve(t, n_prompts));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t n_ids = static_cast<size_t>(n_prompts) * t->cfg.n_pos;
+    B2Q_TRY(cuda_check(cudaMemcpyAsync(t->ids_in.p, ids_host, n_ids * 4, cudaMemcpyHostToDevice, s), "id upload"));
+    B2Q_TRY(b2q_text_encode(t, t->ids_in.as<int32_t>(), n_prompts, t->out_dev.as<float>(), stream));
+    B2Q_TRY(cuda_check(cudaMemcpyAsync(out_host, t->out_dev.p, static_cast<size_t>(n_prompts) * t->cfg.hidden * 4,
+                                       cudaMemcpyDeviceToHost, s),
+                       "embedding download"));
+    return cuda_check(cudaStreamSynchronize(s), "text encode");
+}
+
+size_t b2q_score_scratch_bytes(int32_t n_image, int32_t n_text, int32_t hidden) {
+    if (n_image <= 0 || n_text <= 0 || hidden <= 0) return 0;
+    return (static_cast<size_t>(n_image) + n_text) * hidden * 4;
+}
+
+b2q_status b2q_score(const float* img, int32_t n_image, const float* txt, int32_t n_text, int32_t hidden,
+                     float logit_scale, float logit_bias, float* logits, float* probs, void* scratch, void* stream) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!img || !txt || !scratch || (!logits && !probs)) return set_error(B2Q_ERR_INVALID, "null pointer");
+    if (n_image <= 0 || n_text <= 0 || hidden <= 0) return set_error(B2Q_ERR_SHAPE, "empty score problem");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* na = static_cast<float*>(scratch);
+    float* nb = na + static_cast<int64_t>(n_image) * hidden;
+    l2_normalize_kernel<<<(n_image + 127) / 128, 128, 0, s>>>(img, na, n_image, hidden);
+    count_launch();
+    l2_normalize_kernel<<<(n_text + 127) / 128, 128, 0, s>>>(txt, nb, n_text, hidden);
+    count_launch();
+    dim3 grid((n_text + 15) / 16, (n_image + 15) / 16);
+    score_kernel<<<grid, dim3(16, 16), 0, s>>>(na, n_image, nb, n_text, hidden, logit_scale, logit_bias, logits, probs);
+    count_launch();
+    return cuda_check(cudaGetLastError(), "score launch");
+}
+
+}  // extern "C"

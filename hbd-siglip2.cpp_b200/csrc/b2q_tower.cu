@@ -14,7 +14,7 @@
 //   fc2 GEMM, epilogue (acc + b) + x -> x
 // then post-LN and MEAN pooling or the attention-pool head
 // (build_probe_head, src/siglip2_vision.cpp:249-314).
-#include "b2q_internal.h"
+#include "b2q_tower.h"
 
 #include <cmath>
 #include <cstring>
@@ -99,28 +99,84 @@ __global__ void mean_pool_kernel(const float* __restrict__ x, int H, const Image
     out[static_cast<int64_t>(blockIdx.y) * H + i] = static_cast<float>(__ddiv_rn(acc, n));
 }
 
-struct DevBuf {
-    void* p = nullptr;
-    size_t n = 0;
-    ~DevBuf() {
-        if (p) cudaFree(p);
-    }
-    cudaError_t ensure(size_t bytes) {
-        if (bytes <= n) return cudaSuccess;
-        if (p) cudaFree(p);
-        p = nullptr;
-        n = 0;
-        cudaError_t e = cudaMalloc(&p, bytes);
-        if (e == cudaSuccess) n = bytes;
-        return e;
-    }
-    template <class T>
-    T* as() const {
-        return static_cast<T*>(p);
-    }
-};
-
 }  // namespace
+
+// ---------------------------------------------------------------- shared driver pieces
+b2q_status TensorSet::put(const std::string& n, int32_t ggml_type, const void* host_data, int64_t ne0, int64_t ne1,
+                          bool as_raw, cudaStream_t s) {
+    if (ggml_type == 8) {   // GGML_TYPE_Q8_0: ne0 = K (innermost), ne1 = rows
+        if (ne0 <= 0 || ne1 <= 0 || ne0 % 32) return set_error(B2Q_ERR_SHAPE, "Q8_0 tensor " + n + ": bad shape");
+        if (as_raw) {
+            const size_t bytes = static_cast<size_t>(ne1) * (ne0 / 32) * 34;
+            DevBuf& b = raw_q8[n];
+            B2Q_TRY(cuda_check(b.ensure(bytes), "cudaMalloc(table)"));
+            B2Q_TRY(cuda_check(cudaMemcpyAsync(b.p, host_data, bytes, cudaMemcpyHostToDevice, s), "table upload"));
+            return cuda_check(cudaStreamSynchronize(s), "table upload");
+        }
+        auto it = q8.find(n);
+        if (it != q8.end()) {
+            b2q_weight_release(it->second);
+            q8.erase(it);
+        }
+        b2q_weight* w = nullptr;
+        B2Q_TRY(b2q_weight_register(host_data, ne1, ne0, ne0 / 32 * 34, 1, s, &w));
+        q8[n] = w;
+        return B2Q_OK;
+    }
+    if (ggml_type == 0) {   // GGML_TYPE_F32
+        const size_t bytes = static_cast<size_t>(ne0 * (ne1 > 0 ? ne1 : 1)) * 4;
+        DevBuf& b = f32[n];
+        B2Q_TRY(cuda_check(b.ensure(bytes), "cudaMalloc(tensor)"));
+        B2Q_TRY(cuda_check(cudaMemcpyAsync(b.p, host_data, bytes, cudaMemcpyHostToDevice, s), "tensor upload"));
+        return cuda_check(cudaStreamSynchronize(s), "tensor upload");
+    }
+    return set_error(B2Q_ERR_INVALID, "only GGML_TYPE_F32 (0) and GGML_TYPE_Q8_0 (8) tensors are accepted");
+}
+
+b2q_status gemm(const b2q_weight* w, const void* act, int64_t M, void* y, int kind, const float* bias,
+                const float* residual, void* act_out, int64_t ld_out, cudaStream_t s) {
+    b2q_epilogue e{kind, bias, residual, act_out, ld_out};
+    return b2q_mul_mat_q8_0(w, act, M, y, &e, s);
+}
+
+static std::string blkname(const char* prefix, int l, const char* s) {
+    return std::string(prefix) + "blk." + std::to_string(l) + "." + s;
+}
+
+b2q_status check_blocks(const TensorSet& ts, const char* prefix, int n_layer) {
+    static const char* blk_q8[] = {"attn_qkv.weight", "attn_o.weight", "ffn_up.weight", "ffn_down.weight"};
+    static const char* blk_f[] = {"ln1.weight", "ln1.bias", "attn_qkv.bias", "attn_o.bias", "ln2.weight",
+                                  "ln2.bias", "ffn_up.bias", "ffn_down.bias"};
+    for (int l = 0; l < n_layer; ++l) {
+        for (const char* s : blk_q8)
+            if (!ts.w(blkname(prefix, l, s))) return set_error(B2Q_ERR_INVALID, "missing " + blkname(prefix, l, s));
+        for (const char* s : blk_f)
+            if (!ts.f(blkname(prefix, l, s))) return set_error(B2Q_ERR_INVALID, "missing " + blkname(prefix, l, s));
+    }
+    return B2Q_OK;
+}
+
+b2q_status run_encoder_blocks(const TensorSet& ts, const char* prefix, int n_layer, int n_head, float eps, int64_t T,
+                              int64_t H, float* x, __half* qkv, float* att, void* act_h, void* act_f,
+                              const void* tiles, int n_tiles, bool exact_attention, cudaStream_t s) {
+    for (int l = 0; l < n_layer; ++l) {
+        auto W = [&](const char* n) { return ts.w(blkname(prefix, l, n)); };
+        auto F = [&](const char* n) { return ts.f(blkname(prefix, l, n)); };
+        B2Q_TRY(b2q_ln_quantize_q8_1(x, F("ln1.weight"), F("ln1.bias"), eps, T, H, act_h, nullptr, s));
+        B2Q_TRY(gemm(W("attn_qkv.weight"), act_h, T, qkv, B2Q_EPI_BIAS_F16, F("attn_qkv.bias"), nullptr, nullptr, 0,
+                     s));
+        B2Q_TRY(cuda_check(launch_attention(qkv, 3 * H, qkv + H, 3 * H, qkv + 2 * H, 3 * H, tiles, n_tiles, n_head, att,
+                                            H, s, exact_attention),
+                           "attention launch"));
+        B2Q_TRY(b2q_quantize_q8_1(att, T, H, H, act_h, s));
+        B2Q_TRY(gemm(W("attn_o.weight"), act_h, T, x, B2Q_EPI_BIAS_RESIDUAL, F("attn_o.bias"), x, nullptr, 0, s));
+        B2Q_TRY(b2q_ln_quantize_q8_1(x, F("ln2.weight"), F("ln2.bias"), eps, T, H, act_h, nullptr, s));
+        B2Q_TRY(gemm(W("ffn_up.weight"), act_h, T, nullptr, B2Q_EPI_BIAS_GELU_Q8, F("ffn_up.bias"), nullptr, act_f, 0,
+                     s));
+        B2Q_TRY(gemm(W("ffn_down.weight"), act_f, T, x, B2Q_EPI_BIAS_RESIDUAL, F("ffn_down.bias"), x, nullptr, 0, s));
+    }
+    return B2Q_OK;
+}
 
 }  // namespace b2q
 
@@ -129,57 +185,24 @@ using namespace b2q;
 struct b2q_vision {
     b2q_vision_config cfg{};
     int ffn_pad = 0;
-    std::map<std::string, b2q_weight*> q8;        // projections
-    std::map<std::string, DevBuf> f32;            // biases, LN, tables, probe
+    TensorSet ts;                                 // projections, biases, LN, tables, probe
     // workspace
     int64_t cap_tokens = 0;
     int32_t cap_images = 0;
     DevBuf x, pos, qkv16, attn, act_h, act_f, act_p, imgs, tiles, head_tiles, q16, ha, ha2, patches_in, out_dev;
     std::vector<uint8_t> host_tiles, host_head_tiles;
     bool probe_ready = false;
-    ~b2q_vision() {
-        for (auto& kv : q8) b2q_weight_release(kv.second);
-    }
-    const float* f(const std::string& n) const {
-        auto it = f32.find(n);
-        return it == f32.end() ? nullptr : it->second.as<float>();
-    }
-    const b2q_weight* w(const std::string& n) const {
-        auto it = q8.find(n);
-        return it == q8.end() ? nullptr : it->second;
-    }
+    const float* f(const std::string& n) const { return ts.f(n); }
+    const b2q_weight* w(const std::string& n) const { return ts.w(n); }
 };
 
 namespace {
 
-std::string blk(int l, const char* s) { return "v.blk." + std::to_string(l) + "." + s; }
-
-b2q_status gemm(const b2q_weight* w, const void* act, int64_t M, void* y, int kind, const float* bias,
-                const float* residual, void* act_out, int64_t ld_out, cudaStream_t s) {
-    b2q_epilogue e{kind, bias, residual, act_out, ld_out};
-    return b2q_mul_mat_q8_0(w, act, M, y, &e, s);
-}
-
-#define B2Q_TRY(expr)                    \
-    do {                                 \
-        b2q_status _st = (expr);         \
-        if (_st != B2Q_OK) return _st;   \
-    } while (0)
-
 b2q_status check_loaded(const b2q_vision* v) {
-    static const char* blk_q8[] = {"attn_qkv.weight", "attn_o.weight", "ffn_up.weight", "ffn_down.weight"};
-    static const char* blk_f[] = {"ln1.weight", "ln1.bias", "attn_qkv.bias", "attn_o.bias", "ln2.weight",
-                                  "ln2.bias", "ffn_up.bias", "ffn_down.bias"};
     if (!v->w("v.patch_embd.weight") || !v->f("v.patch_embd.bias") || !v->f("v.position_embd.weight") ||
         !v->f("v.post_ln.weight") || !v->f("v.post_ln.bias"))
         return set_error(B2Q_ERR_INVALID, "vision tower: stem / post-LN tensors missing");
-    for (int l = 0; l < v->cfg.n_layer; ++l) {
-        for (const char* s : blk_q8)
-            if (!v->w(blk(l, s))) return set_error(B2Q_ERR_INVALID, "vision tower: missing " + blk(l, s));
-        for (const char* s : blk_f)
-            if (!v->f(blk(l, s))) return set_error(B2Q_ERR_INVALID, "vision tower: missing " + blk(l, s));
-    }
-    return B2Q_OK;
+    return check_blocks(v->ts, "v.", v->cfg.n_layer);
 }
 
 b2q_status check_head(const b2q_vision* v) {
@@ -223,26 +246,8 @@ b2q_status b2q_vision_set_tensor(b2q_vision* v, const char* name, int32_t ggml_t
     B2Q_REQUIRE_STATE();
     (void) ds;
     if (!v || !name || !host_data) return set_error(B2Q_ERR_INVALID, "null pointer");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     const std::string n(name);
-    if (ggml_type == 8) {   // GGML_TYPE_Q8_0: ne0 = K (innermost), ne1 = N rows
-        auto it = v->q8.find(n);
-        if (it != v->q8.end()) {
-            b2q_weight_release(it->second);
-            v->q8.erase(it);
-        }
-        b2q_weight* w = nullptr;
-        B2Q_TRY(b2q_weight_register(host_data, ne1, ne0, ne0 / 32 * 34, 1, stream, &w));
-        v->q8[n] = w;
-    } else if (ggml_type == 0) {   // GGML_TYPE_F32
-        const size_t bytes = static_cast<size_t>(ne0 * (ne1 > 0 ? ne1 : 1)) * 4;
-        DevBuf& b = v->f32[n];
-        B2Q_TRY(cuda_check(b.ensure(bytes), "cudaMalloc(tensor)"));
-        B2Q_TRY(cuda_check(cudaMemcpyAsync(b.p, host_data, bytes, cudaMemcpyHostToDevice, s), "tensor upload"));
-        B2Q_TRY(cuda_check(cudaStreamSynchronize(s), "tensor upload"));
-    } else {
-        return set_error(B2Q_ERR_INVALID, "only GGML_TYPE_F32 (0) and GGML_TYPE_Q8_0 (8) tensors are accepted");
-    }
+    B2Q_TRY(v->ts.put(n, ggml_type, host_data, ne0, ne1, false, static_cast<cudaStream_t>(stream)));
     if (n.rfind("v.head.", 0) == 0) v->probe_ready = false;
     return B2Q_OK;
 }
@@ -349,24 +354,8 @@ b2q_status b2q_vision_encode(b2q_vision* v, const float* patches, const int32_t*
                  pos, nullptr, 0, s));
 
     // ---- encoder blocks ----
-    for (int l = 0; l < c.n_layer; ++l) {
-        B2Q_TRY(b2q_ln_quantize_q8_1(x, v->f(blk(l, "ln1.weight")), v->f(blk(l, "ln1.bias")), c.eps, T, H,
-                                     v->act_h.p, nullptr, s));
-        B2Q_TRY(gemm(v->w(blk(l, "attn_qkv.weight")), v->act_h.p, T, qkv, B2Q_EPI_BIAS_F16,
-                     v->f(blk(l, "attn_qkv.bias")), nullptr, nullptr, 0, s));
-        B2Q_TRY(cuda_check(launch_attention(qkv, 3 * H, qkv + H, 3 * H, qkv + 2 * H, 3 * H, v->tiles.p, n_tiles,
-                                            c.n_head, att, H, s),
-                           "attention launch"));
-        B2Q_TRY(b2q_quantize_q8_1(att, T, H, H, v->act_h.p, s));
-        B2Q_TRY(gemm(v->w(blk(l, "attn_o.weight")), v->act_h.p, T, x, B2Q_EPI_BIAS_RESIDUAL,
-                     v->f(blk(l, "attn_o.bias")), x, nullptr, 0, s));
-        B2Q_TRY(b2q_ln_quantize_q8_1(x, v->f(blk(l, "ln2.weight")), v->f(blk(l, "ln2.bias")), c.eps, T, H,
-                                     v->act_h.p, nullptr, s));
-        B2Q_TRY(gemm(v->w(blk(l, "ffn_up.weight")), v->act_h.p, T, nullptr, B2Q_EPI_BIAS_GELU_Q8,
-                     v->f(blk(l, "ffn_up.bias")), nullptr, v->act_f.p, 0, s));
-        B2Q_TRY(gemm(v->w(blk(l, "ffn_down.weight")), v->act_f.p, T, x, B2Q_EPI_BIAS_RESIDUAL,
-                     v->f(blk(l, "ffn_down.bias")), x, nullptr, 0, s));
-    }
+    B2Q_TRY(run_encoder_blocks(v->ts, "v.", c.n_layer, c.n_head, c.eps, T, H, x, qkv, att, v->act_h.p, v->act_f.p,
+                               v->tiles.p, n_tiles, false, s));
 
     // ---- post-LN (in place) and its q8_1 planes for the head ----
     B2Q_TRY(b2q_ln_quantize_q8_1(x, v->f("v.post_ln.weight"), v->f("v.post_ln.bias"), c.eps, T, H, v->act_h.p, x, s));

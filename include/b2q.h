@@ -62,7 +62,10 @@ b2q_status b2q_init(int device, int ops_mode);
  *                        the tower bit-reproducible), 0 = tensor cores */
 enum { B2Q_TUNE_GEMM_BN = 1, B2Q_TUNE_TIMEOUT_NS = 2, B2Q_TUNE_ATTN_EXACT = 3 };
 b2q_status b2q_tune(int key, int64_t value);
-/* Reads (and clears) the device error word after synchronising `stream`. */
+/* Reads (and clears) the device error word after synchronising `stream`;
+ * B2Q_ERR_DEVICE when it was set: codes 1-4 = an in-kernel wait expired
+ * (1 TMA data, 2 stage release, 3 MMA commit, 4 accumulator release),
+ * 5 = a token id outside the vocabulary. */
 b2q_status b2q_check_device(void *stream, uint32_t *code_out);
 
 /* ---- weights -------------------------------------------------------------
@@ -70,7 +73,9 @@ b2q_status b2q_check_device(void *stream, uint32_t *code_out);
  * N rows of K (ne[0], a multiple of 32; K-padded tensors pass the padded K),
  * row stride row_bytes (>= K/32*34).  `q8_0` is a device pointer, or a host
  * pointer when src_is_host != 0.  Repacks once into a 16-byte-aligned value
- * plane [N][K] and a scale plane [K/32][N]; the source is not retained.
+ * plane [N][K] and an fp32 scale plane [K/32][N rounded up to 64] (columns
+ * permuted inside each 64-column group for the GEMM epilogue's loads); the
+ * source is not retained.
  * Replaces the per-call raw read in src/cuda/siglip2_custom_mmq.cu:176-199. */
 typedef struct b2q_weight b2q_weight;
 b2q_status b2q_weight_register(const void *q8_0, int64_t N, int64_t K, int64_t row_bytes, int src_is_host,
@@ -198,6 +203,48 @@ b2q_status b2q_vision_encode(b2q_vision *v, const float *patches, const int32_t 
  * and synchronises `stream`. */
 b2q_status b2q_vision_encode_host(b2q_vision *v, const float *patches_host, const int32_t *grid_hw,
                                   int32_t n_images, int32_t pooling, float *out_host, void *stream);
+
+/* ---- text tower ------------------------------------------------------------
+ * Batched counterpart of siglip2::TextEncoder::encode_batch
+ * (src/siglip2_text.cpp:741-932; tensors by the GGUF names it loads at
+ * :485-496 and "t.blk.N.*" at :38).  "t.token_embd.weight" is a Q8_0 table
+ * [vocab][hidden] read row by row (get_rows); every other Q8_0 tensor is a
+ * projection.  A batch is n_prompts rows of n_pos token ids (int32, each in
+ * [0, vocab); an id outside it is replaced by 0 and reported through
+ * b2q_check_device); out receives n_prompts x hidden fp32 embeddings: final
+ * LayerNorm of each prompt's last token, then the head projection + bias.
+ * Attention always runs in the fixed fp32 order of B2Q_TUNE_ATTN_EXACT, so
+ * the embeddings are bit-reproducible. */
+typedef struct b2q_text b2q_text;
+typedef struct b2q_text_config {
+    int32_t hidden;     /* 1152 */
+    int32_t ffn;        /* 4304 */
+    int32_t n_head;     /* 16 (head_dim 72) */
+    int32_t n_layer;    /* 27 */
+    int32_t vocab;      /* 256000 */
+    int32_t n_pos;      /* 64 */
+    float eps;          /* 1e-6 */
+} b2q_text_config;
+b2q_status b2q_text_create(const b2q_text_config *cfg, b2q_text **out);
+b2q_status b2q_text_destroy(b2q_text *t);
+b2q_status b2q_text_set_tensor(b2q_text *t, const char *name, int32_t ggml_type, const void *host_data, int64_t ne0,
+                               int64_t ne1, void *stream);
+b2q_status b2q_text_reserve(b2q_text *t, int32_t max_prompts);
+/* Device in ([n_prompts][n_pos] int32), device out ([n_prompts][hidden]). */
+b2q_status b2q_text_encode(b2q_text *t, const int32_t *ids, int32_t n_prompts, float *out, void *stream);
+/* Host in, host out; synchronises `stream`. */
+b2q_status b2q_text_encode_host(b2q_text *t, const int32_t *ids_host, int32_t n_prompts, float *out_host,
+                                void *stream);
+
+/* ---- image-text scoring -----------------------------------------------------
+ * score_image_text (src/siglip2_score.cpp:90-134) on the device: both sets of
+ * rows L2-normalised in double (+1e-12), logits[i][j] = dot(img_i, txt_j) *
+ * e^{logit_scale} + logit_bias with the dot in double, probs = sigmoid(logits).
+ * All pointers are device pointers; logits or probs may be NULL (not both).
+ * scratch: b2q_score_scratch_bytes(n_image, n_text, hidden) bytes. */
+size_t b2q_score_scratch_bytes(int32_t n_image, int32_t n_text, int32_t hidden);
+b2q_status b2q_score(const float *img, int32_t n_image, const float *txt, int32_t n_text, int32_t hidden,
+                     float logit_scale, float logit_bias, float *logits, float *probs, void *scratch, void *stream);
 
 #ifdef __cplusplus
 }

@@ -668,7 +668,7 @@ int orc_text_encode(const orc_text_weights *W, const int32_t *ids, int64_t n_pro
 }
 
 void orc_score(const float *img, int64_t I, const float *txt, int64_t J, int64_t H,
-               float logit_scale, float logit_bias, float *out) {
+               float logit_scale, float logit_bias, float *logits, float *out) {
     float *a = (float *) malloc((size_t) I * H * sizeof(float));
     float *b = (float *) malloc((size_t) J * H * sizeof(float));
     memcpy(a, img, (size_t) I * H * sizeof(float));
@@ -683,7 +683,9 @@ void orc_score(const float *img, int64_t I, const float *txt, int64_t J, int64_t
             float inv = (float) (1.0 / (sqrt(sumsq) + 1e-12));
             for (int64_t c = 0; c < H; ++c) row[c] *= inv;
         }
-    const float scale = expf(logit_scale);
+    /* exp and the sigmoid's division are the library's own (orc_expf,
+     * orc_div), the exponent clamped to 80 as in orc_gelu */
+    const float scale = orc_expf(logit_scale);
     #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < I; ++i)
         for (int64_t j = 0; j < J; ++j) {
@@ -691,8 +693,9 @@ void orc_score(const float *img, int64_t I, const float *txt, int64_t J, int64_t
             for (int64_t c = 0; c < H; ++c) dot += (double) a[i * H + c] * (double) b[j * H + c];
             float logit = (float) (dot * (double) scale + (double) logit_bias);
             float p;
-            if (logit >= 0.0f) { float e = expf(-logit); p = 1.0f / (1.0f + e); }
-            else               { float e = expf(logit);  p = e / (1.0f + e); }
+            if (logit >= 0.0f) { float e = orc_expf(logit < 80.0f ? -logit : -80.0f); p = orc_div(1.0f, 1.0f + e); }
+            else               { float e = orc_expf(logit > -80.0f ? logit : -80.0f); p = orc_div(e, 1.0f + e); }
+            if (logits) logits[i * J + j] = logit;
             out[i * J + j] = p;
         }
     free(a);

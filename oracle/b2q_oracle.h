@@ -135,9 +135,11 @@ int orc_text_encode(const orc_text_weights *W, const int32_t *ids, int64_t n_pro
                     int quant_act, float *out);
 
 /* Sigmoid scores (siglip2_score.cpp:78-134): img [I][H], txt [J][H] ->
- * out [I][J] = sigmoid(exp(logit_scale) * <img_i/|img_i|, txt_j/|txt_j|> + bias). */
+ * out [I][J] = sigmoid(exp(logit_scale) * <img_i/|img_i|, txt_j/|txt_j|> + bias),
+ * norms and dots in double; logits (may be NULL) receives the pre-sigmoid
+ * values.  exp and the division are orc_expf / orc_div. */
 void orc_score(const float *img, int64_t I, const float *txt, int64_t J, int64_t H,
-               float logit_scale, float logit_bias, float *out);
+               float logit_scale, float logit_bias, float *logits, float *out);
 
 #ifdef __cplusplus
 }

@@ -57,7 +57,7 @@ def _declare(L):
     L.orc_pos_resize.argtypes = [P, I64, I64, I64, I64, P]
     L.orc_vision_encode.argtypes = [P, P, I64, I64, C.c_int, C.c_int, P]
     L.orc_text_encode.argtypes = [P, P, I64, C.c_int, P]
-    L.orc_score.argtypes = [P, I64, P, I64, I64, C.c_float, C.c_float, P]
+    L.orc_score.argtypes = [P, I64, P, I64, I64, C.c_float, C.c_float, P, P]
 
 
 def _p(a: np.ndarray):
@@ -251,10 +251,11 @@ def text_encode(ck, ids: np.ndarray, quant_act: bool = True) -> np.ndarray:
     return out
 
 
-def score(img: np.ndarray, txt: np.ndarray, logit_scale: float, logit_bias: float) -> np.ndarray:
+def score(img: np.ndarray, txt: np.ndarray, logit_scale: float, logit_bias: float, with_logits: bool = False):
     img = np.ascontiguousarray(img, np.float32)
     txt = np.ascontiguousarray(txt, np.float32)
     out = np.empty((img.shape[0], txt.shape[0]), np.float32)
+    logits = np.empty_like(out) if with_logits else None
     lib().orc_score(_p(img), img.shape[0], _p(txt), txt.shape[0], img.shape[1],
-                    float(logit_scale), float(logit_bias), _p(out))
-    return out
+                    float(logit_scale), float(logit_bias), _p(logits) if with_logits else None, _p(out))
+    return (out, logits) if with_logits else out

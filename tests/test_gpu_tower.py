@@ -5,8 +5,9 @@ Two bars:
 * exact attention mode (B2Q_TUNE_ATTN_EXACT): the whole tower, 27 layers and
   both poolings, is bit-identical to the oracle — every kernel follows the
   oracle's fixed fp32 operation order;
-* default tensor-core attention (fp16 Q and P, fp32 accumulation, as ggml's
-  flash attention): cosine >= 0.9999.  Any attention
+* default tensor-core attention (fp16 Q, K, V as in the reference, the
+  softmax probabilities carried as two fp16 halves, fp32 accumulation):
+  cosine >= 0.9999.  Any attention
   that is not bit-reproducible moves some q8_1 rounding decisions downstream;
   over 27 layers that moves pooled values by up to ~0.03 (measured on the CPU
   between two oracle attention precisions: 0.023-0.028 on values of ~2), so
