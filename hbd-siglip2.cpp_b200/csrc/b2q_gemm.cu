@@ -360,9 +360,10 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
         tc_fence_after();
         tmem_ld_16x256b_x8(taddr0 + acc_ring.idx * Cfg::BN, ra);
         int kb = 0;
+        bool stage_ready = false;   // set by an early probe of the next stage's barrier
         for (int st = 0; st < nst; ++st) {
             const uint32_t s = st_ring.idx;
-            if (!mbar_wait(bar_at(sm.full, s), st_ring.phase, sm.abort_flag, p.timeout_ns)) {
+            if (!stage_ready && !mbar_wait(bar_at(sm.full, s), st_ring.phase, sm.abort_flag, p.timeout_ns)) {
                 raise_error(p.err, sm.abort_flag, kDevTimeoutFull);
                 return false;
             }
@@ -371,6 +372,7 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
             // dW[j][slot]: this thread's 16-byte vectors sit at slots 16i + 4q of each 64-column chunk
             const uint32_t sdw = sbase + Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES + (col0 + 4 * q) * 4;
             const int nkb = min(Cfg::KBS, p.Kb - st * Cfg::KBS);
+            stage_ready = false;
 #pragma unroll
             for (int j = 0; j < Cfg::KBS; ++j) {
                 if (j < nkb) {
@@ -389,6 +391,9 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
 #pragma unroll
                         for (int i = 0; i < 4; ++i) wv[cc][i] = lds_v4_f32(w2 + (cc * 64 + 16 * i) * 4);
                     const bool has_next = kb + 1 < p.Kb;
+                    // the next accumulator's barrier is probed one chunk before its first
+                    // load, so the probe's round trip overlaps this chunk's arithmetic
+                    bool next_ready = false;
 #pragma unroll
                     for (int c = 0; c < Cfg::CH; ++c) {
                         uint32_t(&cur)[32] = (c & 1) ? rb : ra;
@@ -400,7 +405,8 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
                             if (lane == 0) mbar_arrive(bar_at(sm.tempty, acc_ring.idx));
                             acc_ring.next();
                             if (has_next) {
-                                if (!mbar_wait(bar_at(sm.tfull, acc_ring.idx), acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
+                                if (!next_ready &&
+                                    !mbar_wait(bar_at(sm.tfull, acc_ring.idx), acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
                                     raise_error(p.err, sm.abort_flag, kDevTimeoutTmemFull);
                                     return false;
                                 }
@@ -412,6 +418,16 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
                             tmem_ld_16x256b_x8(taddr0 + acc_ring.idx * Cfg::BN +
                                                    (static_cast<uint32_t>((c1 & 1) * 16) << 16) + (c1 >> 1) * 64,
                                                nxt);
+                            if (c == Cfg::CH - 2 && has_next) {
+                                Ring<Cfg::NBUF> nb = acc_ring;
+                                nb.next();
+                                next_ready = mbar_test_wait(bar_at(sm.tfull, nb.idx), nb.phase);
+                                if (j == nkb - 1) {   // the next block starts the next stage
+                                    Ring<Cfg::STAGES> ns = st_ring;
+                                    ns.next();
+                                    stage_ready = mbar_test_wait(bar_at(sm.full, ns.idx), ns.phase);
+                                }
+                            }
                         }
                         if constexpr (kDump) {
                             const int sl = c & 1, cc = c >> 1;
