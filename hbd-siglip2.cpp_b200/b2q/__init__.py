@@ -30,6 +30,8 @@ EXPORTS = [
     "b2q_vision_encode", "b2q_vision_encode_host",
     "b2q_text_create", "b2q_text_destroy", "b2q_text_set_tensor", "b2q_text_reserve", "b2q_text_encode",
     "b2q_text_encode_host", "b2q_score_scratch_bytes", "b2q_score",
+    "b2q_gguf_open", "b2q_gguf_close", "b2q_gguf_n_tensors", "b2q_gguf_tensor", "b2q_gguf_scalar_f32",
+    "b2q_vision_load_gguf", "b2q_text_load_gguf",
 ]
 
 
@@ -106,6 +108,15 @@ def lib():
         L.b2q_score_scratch_bytes.argtypes = [C.c_int32, C.c_int32, C.c_int32]
         L.b2q_score_scratch_bytes.restype = C.c_size_t
         L.b2q_score.argtypes = [P, C.c_int32, P, C.c_int32, C.c_int32, C.c_float, C.c_float, P, P, P, P]
+        L.b2q_gguf_open.argtypes = [C.c_char_p, C.POINTER(P)]
+        L.b2q_gguf_close.argtypes = [P]
+        L.b2q_gguf_n_tensors.argtypes = [P]
+        L.b2q_gguf_n_tensors.restype = I64
+        L.b2q_gguf_tensor.argtypes = [P, I64, C.POINTER(C.c_char_p), C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                      C.POINTER(I64), C.POINTER(P)]
+        L.b2q_gguf_scalar_f32.argtypes = [P, C.c_char_p, C.POINTER(C.c_float)]
+        L.b2q_vision_load_gguf.argtypes = [P, P, P]
+        L.b2q_text_load_gguf.argtypes = [P, P, P]
         for name in EXPORTS:
             fn = getattr(L, name)
             if name not in ("b2q_last_error", "b2q_abi_version", "b2q_act_bytes", "b2q_attention_scratch_bytes",
@@ -291,6 +302,10 @@ class VisionTower:
     def reserve(self, max_tokens: int, max_images: int):
         check(lib().b2q_vision_reserve(self.handle, max_tokens, max_images))
 
+    def load_gguf(self, g: "Gguf", stream=None):
+        """Every "v." tensor of an open GGUF file (b2q_vision_load_gguf)."""
+        check(lib().b2q_vision_load_gguf(self.handle, g.handle, _stream(stream)))
+
     def encode(self, patches, grids, pooling=POOL_PROBE, out=None, stream=None):
         """patches: torch CUDA fp32 [T][patch_dim] (images back to back); grids: [(h, w), ...]."""
         import torch
@@ -354,6 +369,10 @@ class TextTower:
     def reserve(self, max_prompts: int):
         check(lib().b2q_text_reserve(self.handle, max_prompts))
 
+    def load_gguf(self, g: "Gguf", stream=None):
+        """Every "t." tensor of an open GGUF file (b2q_text_load_gguf)."""
+        check(lib().b2q_text_load_gguf(self.handle, g.handle, _stream(stream)))
+
     def encode(self, ids, out=None, stream=None):
         """ids: torch CUDA int32 [n_prompts][n_pos]."""
         import torch
@@ -394,3 +413,39 @@ def score(img, txt, logit_scale: float, logit_bias: float, logits=True, probs=Tr
     check(lib().b2q_score(_ptr(img), I, _ptr(txt), J, H, float(logit_scale), float(logit_bias), _ptr(lg), _ptr(pr),
                           _ptr(scratch), _stream(stream)))
     return lg, pr
+
+
+class Gguf:
+    """A GGUF checkpoint mapped by the library (b2q_gguf_*)."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().b2q_gguf_open(str(path).encode(), C.byref(h)))
+        self.handle = h
+
+    def tensors(self):
+        """[(name, ggml_type, ne tuple, data address)] in file order."""
+        out = []
+        for i in range(int(lib().b2q_gguf_n_tensors(self.handle))):
+            name, typ, nd = C.c_char_p(), C.c_int32(), C.c_int32()
+            ne = (I64 * 4)()
+            data = C.c_void_p()
+            check(lib().b2q_gguf_tensor(self.handle, i, C.byref(name), C.byref(typ), C.byref(nd), ne, C.byref(data)))
+            out.append((name.value.decode(), typ.value, tuple(ne[: nd.value]), data.value))
+        return out
+
+    def scalar(self, name: str) -> float:
+        v = C.c_float()
+        check(lib().b2q_gguf_scalar_f32(self.handle, name.encode(), C.byref(v)))
+        return v.value
+
+    def close(self):
+        if self.handle:
+            lib().b2q_gguf_close(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

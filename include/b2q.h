@@ -246,6 +246,28 @@ size_t b2q_score_scratch_bytes(int32_t n_image, int32_t n_text, int32_t hidden);
 b2q_status b2q_score(const float *img, int32_t n_image, const float *txt, int32_t n_text, int32_t hidden,
                      float logit_scale, float logit_bias, float *logits, float *probs, void *scratch, void *stream);
 
+/* ---- GGUF checkpoints -------------------------------------------------------
+ * Counterpart of GGUFLoader (src/gguf_loader.cpp:205-337).  b2q_gguf_open maps
+ * a GGUF v2/v3 file read-only and parses its tensor table (no GPU needed);
+ * tensor data pointers stay valid until b2q_gguf_close.  The tower loaders
+ * hand every "v." / "t." tensor to b2q_vision_set_tensor / b2q_text_set_tensor:
+ * biases, LayerNorm parameters, position tables and the probe as F32 (F16 and
+ * BF16 widened), every other ".weight" as Q8_0 (stored Q8_0: as is; stored
+ * F16/BF16/F32: quantized here with the ggml Q8_0 rule, K zero-padded to a
+ * multiple of 32, as the reference converts F16 at load, gguf_loader.cpp:
+ * 297-318).  Scoring parameters are [1]-shaped tensors ("mm.logit_scale",
+ * "mm.logit_bias", src/siglip2_score.cpp:25-72): b2q_gguf_scalar_f32. */
+typedef struct b2q_gguf b2q_gguf;
+b2q_status b2q_gguf_open(const char *path, b2q_gguf **out);
+b2q_status b2q_gguf_close(b2q_gguf *g);
+int64_t b2q_gguf_n_tensors(const b2q_gguf *g);
+/* ne: 4 entries (unused dimensions 1); data points into the mapped file. */
+b2q_status b2q_gguf_tensor(const b2q_gguf *g, int64_t i, const char **name, int32_t *ggml_type, int32_t *n_dims,
+                           int64_t *ne, const void **data);
+b2q_status b2q_gguf_scalar_f32(const b2q_gguf *g, const char *name, float *out);
+b2q_status b2q_vision_load_gguf(b2q_vision *v, const b2q_gguf *g, void *stream);
+b2q_status b2q_text_load_gguf(b2q_text *t, const b2q_gguf *g, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
