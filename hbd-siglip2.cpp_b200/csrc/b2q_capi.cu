@@ -117,6 +117,9 @@ b2q_status b2q_tune(int key, int64_t value) {
         case B2Q_TUNE_ATTN_EXACT:
             ds->attn_exact = value ? 1 : 0;
             return B2Q_OK;
+        case B2Q_TUNE_TEST_STALL:
+            ds->test_stall = value ? 1 : 0;
+            return B2Q_OK;
         default:
             return set_error(B2Q_ERR_INVALID, "unknown tuning key");
     }

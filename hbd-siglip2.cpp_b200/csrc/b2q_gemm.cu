@@ -75,6 +75,7 @@ struct GemmParams {
     int32_t* dump;
     uint32_t* err;
     uint64_t timeout_ns;
+    int stall;          // failure-path test: the producer issues nothing, so waits expire
 };
 
 __device__ __forceinline__ void raise_error(uint32_t* err, volatile uint32_t* abort_flag, uint32_t code) {
@@ -140,6 +141,7 @@ __device__ bool run_producer(const Smem& sm, const CUtensorMap* tmA, const CUten
     using Cfg = GemmCfg<kOps, kBN>;
     const int num_tiles = p.m_tiles * p.n_tiles;
     const int nst = (p.Kb + Cfg::KBS - 1) / Cfg::KBS;
+    if (p.stall) return true;   // nothing issued: the consumers' bounded waits run out
     Ring<Cfg::STAGES> st_ring;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
         const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles;
@@ -531,6 +533,9 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     } else {
         warpgroup_reg_alloc<Cfg::EPI_REGS>();
         run_epilogue<kOps, kBN, kDump>(sm, tmem_base, p, warp, lane);
+        // an epilogue that gave up on an expired wait may still have a TMEM
+        // load in flight: let it land before TMEM is released
+        tmem_ld_wait();
         tc_fence_before();
     }
 
@@ -583,6 +588,7 @@ static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s) {
     p.dump = a.dump;
     p.err = ds->err;
     p.timeout_ns = ds->timeout_ns;
+    p.stall = ds->test_stall;
     if (a.epi == B2Q_EPI_BIAS_GELU_Q8) {
         const ActLayout O = act_layout(a.M, w->N, kOps);
         p.q_out = a.act_out;
