@@ -188,6 +188,43 @@ static inline void q8_1_block(const float *v, int8_t *q, float *d) {
     }
 }
 
+/* Alternative activation rules (ggml-CUDA's own q8_1 source is absent here,
+ * so the conventions it might use are kept selectable for a later check
+ * against it): 0 = the rule above (x * (127/a), half to even; what the GPU
+ * kernels do), 1 = x * (127/a) rounded half away from zero, 2 = x / d
+ * (d = a/127) half to even, 3 = x * (1/d) half away from zero (the ggml CPU
+ * Q8_0 convention applied to activations). */
+static inline int8_t q8_1_round(float v, float a, float d, int rule) {
+    float r;
+    if (a == 0.0f) return 0;
+    switch (rule) {
+        case 1:  r = roundf(v * (127.0f / a)); break;
+        case 2:  r = rintf(v / d); break;
+        case 3:  r = roundf(v * (1.0f / d)); break;
+        default: r = rintf(v * (127.0f / a)); break;
+    }
+    if (r > 127.0f) r = 127.0f;
+    if (r < -128.0f) r = -128.0f;
+    return (int8_t) r;
+}
+
+void orc_quantize_q8_1_rule(const float *x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
+                            int8_t *qs, float *d, int rule) {
+    const int64_t Kb = Kp / 32;
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t kb = 0; kb < Kb; ++kb) {
+            float v[32], a = 0.0f;
+            for (int j = 0; j < 32; ++j) {
+                int64_t k = kb * 32 + j;
+                v[j] = (k < K) ? x[m * ldx + k] : 0.0f;
+                a = fmaxf(a, fabsf(v[j]));
+            }
+            const float dd = a / 127.0f;
+            d[m * Kb + kb] = dd;
+            for (int j = 0; j < 32; ++j) qs[m * Kp + kb * 32 + j] = q8_1_round(v[j], a, dd, rule);
+        }
+}
+
 void orc_quantize_q8_1(const float *x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
                        int8_t *qs, float *d) {
     const int64_t Kb = Kp / 32;

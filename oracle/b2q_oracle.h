@@ -59,6 +59,10 @@ void orc_dequantize_q8_0(const uint8_t *w, int64_t N, int64_t Kp, float *out);
 /* q8_1 activation planes: qs [M][Kp] int8, d [M][Kp/32] fp32. */
 void orc_quantize_q8_1(const float *x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
                        int8_t *qs, float *d);
+/* The same with a selectable rounding convention (0 = the default above;
+ * 1 = half away from zero; 2 = x/d; 3 = x*(1/d) half away), see b2q_oracle.c. */
+void orc_quantize_q8_1_rule(const float *x, int64_t M, int64_t K, int64_t ldx, int64_t Kp,
+                            int8_t *qs, float *d, int rule);
 
 /* ---- GEMM --------------------------------------------------------------- */
 /* y[m][n] = sum_kb dw[n,kb]*dx[m,kb]*S[m,n,kb]  (canonical order above).

@@ -46,6 +46,7 @@ def _declare(L):
     L.orc_div.argtypes = [C.c_float, C.c_float]; L.orc_div.restype = C.c_float
     L.orc_gelu.argtypes = [C.c_float]; L.orc_gelu.restype = C.c_float
     L.orc_gelu_n.argtypes = [C.c_void_p, C.c_int64, C.c_void_p]; L.orc_gelu_n.restype = None
+    L.orc_quantize_q8_1_rule.argtypes = [P, I64, I64, I64, I64, P, P, C.c_int]
     L.orc_num_threads.restype = C.c_int
     L.orc_set_num_threads.argtypes = [C.c_int]
     L.orc_quantize_q8_0.argtypes = [P, I64, I64, I64, P]
@@ -110,14 +111,18 @@ def dequantize_q8_0(q: np.ndarray, kp: int) -> np.ndarray:
     return out
 
 
-def quantize_q8_1(x: np.ndarray, kp: int | None = None):
-    """-> (qs int8 [M][Kp], d fp32 [M][Kp/32])"""
+def quantize_q8_1(x: np.ndarray, kp: int | None = None, rule: int | None = None):
+    """-> (qs int8 [M][Kp], d fp32 [M][Kp/32]); rule selects an alternative
+    rounding convention (orc_quantize_q8_1_rule), None = the default."""
     x = np.ascontiguousarray(x, np.float32)
     m, k = x.shape
     kp = k if kp is None else kp
     qs = np.empty((m, kp), np.int8)
     d = np.empty((m, kp // 32), np.float32)
-    lib().orc_quantize_q8_1(_p(x), m, k, k, kp, _p(qs), _p(d))
+    if rule is None:
+        lib().orc_quantize_q8_1(_p(x), m, k, k, kp, _p(qs), _p(d))
+    else:
+        lib().orc_quantize_q8_1_rule(_p(x), m, k, k, kp, _p(qs), _p(d), int(rule))
     return qs, d
 
 

@@ -146,6 +146,32 @@ def test_oracle_reproduces_gemm_golden_vectors(oracle):
     assert z["qs0"].min() == 0 and z["qs0"].max() == 0 and z["d0"].max() == 0.0   # all-zero block
 
 
+def test_q8_1_rounding_conventions(oracle):
+    """The selectable q8_1 conventions agree everywhere except where they must
+    differ: exact .5 ties (half-even vs half-away) and the last-bit
+    differences between x*(127/a) and x/(a/127).  Rule 0 is the default (and
+    what the GPU kernels reproduce bit for bit)."""
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((64, 1152)).astype(np.float32)
+    q0, d0 = oracle.quantize_q8_1(x)
+    qr, dr = oracle.quantize_q8_1(x, rule=0)
+    np.testing.assert_array_equal(q0, qr)
+    np.testing.assert_array_equal(d0, dr)
+    for rule in (1, 2, 3):
+        q, d = oracle.quantize_q8_1(x, rule=rule)
+        np.testing.assert_array_equal(d, d0)
+        assert np.abs(q.astype(int) - q0.astype(int)).max() <= 1
+        assert (q != q0).mean() < 1e-3
+    # ties: 127 at the max, so x * (127/a) lands exactly on k + 0.5
+    t = np.zeros((1, 32), np.float32)
+    t[0, 0] = 127.0
+    t[0, 1:5] = [0.5, 1.5, -2.5, 3.5]
+    q_even, _ = oracle.quantize_q8_1(t, rule=0)
+    q_away, _ = oracle.quantize_q8_1(t, rule=1)
+    assert q_even[0, 1:5].tolist() == [0, 2, -2, 4]
+    assert q_away[0, 1:5].tolist() == [1, 2, -3, 4]
+
+
 def test_layernorm_matches_float64(oracle):
     rng = np.random.default_rng(4)
     x = rng.standard_normal((9, 1152)).astype(np.float32) * 3 + 1
