@@ -224,6 +224,124 @@ def profile_gemm(tokens):
     return 0
 
 
+def _events_ms(fn, reps, warm=2):
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def suite(args):
+    """BASELINE configs 1, 2, 3 and 5 on one GPU, one JSON line each (config 4
+    is the default bench line).  CPU counterparts: the CPU restatement (oracle/)
+    on all host threads, on the samples named in each line."""
+    import math
+    import torch
+    import b2q
+    from b2q import synth
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    O.build()
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
+    b2q.init(0)
+    out = []
+
+    def emit(d):
+        print(json.dumps(d), flush=True)
+        out.append(d)
+
+    i8 = int8_peak_tops()
+    cfg = synth.TowerConfig()
+    rng = np.random.default_rng(0)
+
+    # ---- config 2: GEMM sweep (ggml_mul_mat = quantize + GEMM, and GEMM alone)
+    for (N, K) in [(1152, 1152), (3456, 1152), (4304, 1152), (1152, 4304)]:
+        Kp = (K + 31) // 32 * 32
+        wq = synth.quantize_q8_0((rng.standard_normal((N, K)) * 0.02).astype(np.float32), Kp)
+        W = b2q.Weight(wq, N, Kp)
+        xs = rng.standard_normal((64, K)).astype(np.float32)
+        t = time.perf_counter()
+        qs, d = O.quantize_q8_1(xs, Kp)
+        O.gemm_q8(wq, N, Kp, qs, d)
+        cpu_gops = 2.0 * 64 * N * K / (time.perf_counter() - t) / 1e9
+        for M in (729, 4096, 65536):
+            x = torch.randn((M, K), device="cuda")
+            act = b2q.act_empty(M, Kp)
+            scratch = b2q.act_empty(M, Kp)
+            y = torch.empty((M, N), device="cuda")
+            b2q.quantize_q8_1(x, act, M, K)
+            ms_gemm = _events_ms(lambda: b2q.mul_mat(W, act, M, y), 10)
+            ms_full = _events_ms(lambda: b2q.mul_mat_f32(W, x, M, K, y, scratch), 10)
+            tops = 2.0 * M * N * K / (ms_gemm * 1e-3) / 1e12
+            emit({"config": "C2 GEMM", "M": M, "N": N, "K": K, "gemm_ms": ms_gemm, "gemm_tops": tops,
+                  "mul_mat_ms": ms_full, "mul_mat_tops": 2.0 * M * N * K / (ms_full * 1e-3) / 1e12,
+                  "frac_int8": tops / i8 if i8 else None, "int8_peak_measured": i8,
+                  "cpu_gops": cpu_gops, "cpu_sample": f"M=64 rows, {cores} threads"})
+            del x, act, scratch, y
+        W.release()
+    b2q.check_device()
+
+    # ---- config 1: vision tower, batch 1, 27 x 27 patches
+    vck = synth.vision_checkpoint(cfg, seed=0)
+    vt = b2q.VisionTower(cfg)
+    vt.load(vck)
+    p1 = synth.patches(729, cfg.patch_dim, seed=1)
+    pd = torch.from_numpy(p1).cuda()
+    emb = torch.empty((1, cfg.hidden), device="cuda")
+    ms1 = _events_ms(lambda: vt.encode(pd, [(27, 27)], b2q.POOL_PROBE, out=emb), 20, warm=3)
+    t = time.perf_counter()
+    O.vision_encode(vck, p1, 27, 27, pooling=1)
+    cpu1 = 1.0 / (time.perf_counter() - t)
+    emit({"config": "C1 vision batch 1, 729 patches", "ms_per_image": ms1, "images_per_s": 1e3 / ms1,
+          "int8_tops": 604.5e9 / (ms1 * 1e-3) / 1e12, "cpu_images_per_s": cpu1, "cpu_cores": cores})
+
+    # ---- config 3: text tower, 5 prompts x 64
+    tck = synth.text_checkpoint(cfg, seed=0)
+    tt = b2q.TextTower(cfg)
+    tt.load(tck)
+    ids = synth.token_ids(5, cfg.n_pos, cfg.vocab, seed=1)
+    idd = torch.from_numpy(ids).cuda()
+    temb = torch.empty((5, cfg.hidden), device="cuda")
+    ms3 = _events_ms(lambda: tt.encode(idd, out=temb), 20, warm=3)
+    t = time.perf_counter()
+    O.text_encode(tck, ids)
+    cpu3 = 5.0 / (time.perf_counter() - t)
+    emit({"config": "C3 text 5 x 64", "ms_per_batch": ms3, "prompts_per_s": 5e3 / ms3,
+          "cpu_prompts_per_s": cpu3, "cpu_cores": cores})
+
+    # ---- config 5: zero-shot, 2048 images x 729 patches vs 1000 prompts, one GPU
+    n_img, n_txt, chunk = 2048, 1000, 512
+    pchunk = torch.from_numpy(np.concatenate([synth.patches(729, cfg.patch_dim, seed=10 + i)
+                                              for i in range(chunk)])).cuda()
+    img = torch.empty((n_img, cfg.hidden), device="cuda")
+    ids5 = torch.from_numpy(synth.token_ids(n_txt, cfg.n_pos, cfg.vocab, seed=2)).cuda()
+    txt = torch.empty((n_txt, cfg.hidden), device="cuda")
+    vt.reserve(chunk * 729, chunk)
+    tt.reserve(n_txt)
+
+    def zero_shot():
+        for c in range(0, n_img, chunk):
+            vt.encode(pchunk, [(27, 27)] * chunk, b2q.POOL_PROBE, out=img[c:c + chunk])
+        tt.encode(ids5, out=txt)
+        return b2q.score(img, txt, math.log(10.0), -10.0, logits=False)
+
+    ms5 = _events_ms(zero_shot, 2, warm=1)
+    b2q.check_device()
+    emit({"config": "C5 zero-shot 2048 images x 1000 prompts (1 GPU)", "ms": ms5,
+          "images_per_s": n_img * 1e3 / ms5, "note": "patches of the 512-image chunk reused for all 4 chunks"})
+    if args.out:
+        Path(args.out).write_text("".join(json.dumps(d) + "\n" for d in out))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -234,11 +352,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="TOKENS",
                     help="only run the fc1 GEMM (GELU->q8_1 epilogue) at this token count, for ncu captures")
+    ap.add_argument("--suite", action="store_true", help="configs 1, 2, 3 and 5 on one GPU (JSON lines)")
+    ap.add_argument("--out", default="", help="--suite: also write the JSON lines to this file")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
     if args.profile_gemm:
         return profile_gemm(args.profile_gemm)
+    if args.suite:
+        return suite(args)
 
     import torch
     import torch.distributed as dist

@@ -192,6 +192,10 @@ struct b2q_vision {
     DevBuf x, pos, qkv16, attn, act_h, act_f, act_p, imgs, tiles, head_tiles, q16, ha, ha2, patches_in, out_dev;
     std::vector<uint8_t> host_tiles, host_head_tiles;
     bool probe_ready = false;
+    // batch geometry whose tables are on the device (a repeated geometry
+    // skips the upload and its stream synchronisation)
+    std::vector<int32_t> tables_for;
+    int n_tiles = 0, n_htiles = 0;
     const float* f(const std::string& n) const { return ts.f(n); }
     const b2q_weight* w(const std::string& n) const { return ts.w(n); }
 };
@@ -275,6 +279,7 @@ b2q_status b2q_vision_reserve(b2q_vision* v, int64_t max_tokens, int32_t max_ima
     B2Q_TRY(cuda_check(v->out_dev.ensure(static_cast<size_t>(max_images) * H * 4), "cudaMalloc(out)"));
     v->host_tiles.resize(attn_tiles_bytes(static_cast<int>(tiles)));
     v->host_head_tiles.resize(attn_tiles_bytes(max_images));
+    v->tables_for.clear();   // device tables may have moved
     v->cap_tokens = T;
     v->cap_images = max_images;
     return B2Q_OK;
@@ -309,22 +314,33 @@ b2q_status b2q_vision_encode(b2q_vision* v, const float* patches, const int32_t*
     if (T > v->cap_tokens || n_images > v->cap_images)
         B2Q_TRY(b2q_vision_reserve(v, T > v->cap_tokens ? T : v->cap_tokens,
                                    n_images > v->cap_images ? n_images : v->cap_images));
-    const int n_tiles = attn_build_tiles(off.data(), len.data(), off.data(), len.data(), off.data(), n_images,
-                                         v->host_tiles.data(), static_cast<int>(v->host_tiles.size() / attn_tiles_bytes(1)));
-    const int n_htiles = attn_build_tiles(zero.data(), one.data(), off.data(), len.data(), oidx.data(), n_images,
-                                          v->host_head_tiles.data(),
-                                          static_cast<int>(v->host_head_tiles.size() / attn_tiles_bytes(1)));
-    if (n_tiles < 0 || n_htiles < 0) return set_error(B2Q_ERR_SHAPE, "attention tile table overflow");
-    B2Q_TRY(cuda_check(cudaMemcpyAsync(v->imgs.p, imgs.data(), n_images * sizeof(ImageDesc), cudaMemcpyHostToDevice, s),
-                       "image table upload"));
-    B2Q_TRY(cuda_check(cudaMemcpyAsync(v->tiles.p, v->host_tiles.data(), attn_tiles_bytes(n_tiles),
-                                       cudaMemcpyHostToDevice, s),
-                       "tile table upload"));
-    B2Q_TRY(cuda_check(cudaMemcpyAsync(v->head_tiles.p, v->host_head_tiles.data(), attn_tiles_bytes(n_htiles),
-                                       cudaMemcpyHostToDevice, s),
-                       "head tile table upload"));
-    // keep the host tables alive until the copies have been consumed
-    B2Q_TRY(cuda_check(cudaStreamSynchronize(s), "table upload"));
+    const bool same = v->tables_for.size() == static_cast<size_t>(2 * n_images) &&
+                      std::memcmp(v->tables_for.data(), grid_hw, 2 * n_images * sizeof(int32_t)) == 0;
+    if (!same) {
+        v->n_tiles = attn_build_tiles(off.data(), len.data(), off.data(), len.data(), off.data(), n_images,
+                                      v->host_tiles.data(),
+                                      static_cast<int>(v->host_tiles.size() / attn_tiles_bytes(1)));
+        v->n_htiles = attn_build_tiles(zero.data(), one.data(), off.data(), len.data(), oidx.data(), n_images,
+                                       v->host_head_tiles.data(),
+                                       static_cast<int>(v->host_head_tiles.size() / attn_tiles_bytes(1)));
+        if (v->n_tiles < 0 || v->n_htiles < 0) {
+            v->tables_for.clear();
+            return set_error(B2Q_ERR_SHAPE, "attention tile table overflow");
+        }
+        B2Q_TRY(cuda_check(cudaMemcpyAsync(v->imgs.p, imgs.data(), n_images * sizeof(ImageDesc),
+                                           cudaMemcpyHostToDevice, s),
+                           "image table upload"));
+        B2Q_TRY(cuda_check(cudaMemcpyAsync(v->tiles.p, v->host_tiles.data(), attn_tiles_bytes(v->n_tiles),
+                                           cudaMemcpyHostToDevice, s),
+                           "tile table upload"));
+        B2Q_TRY(cuda_check(cudaMemcpyAsync(v->head_tiles.p, v->host_head_tiles.data(), attn_tiles_bytes(v->n_htiles),
+                                           cudaMemcpyHostToDevice, s),
+                           "head tile table upload"));
+        // keep the host tables alive until the copies have been consumed
+        B2Q_TRY(cuda_check(cudaStreamSynchronize(s), "table upload"));
+        v->tables_for.assign(grid_hw, grid_hw + 2 * n_images);
+    }
+    const int n_tiles = v->n_tiles, n_htiles = v->n_htiles;
 
     if (pooling == B2Q_POOL_PROBE && !v->probe_ready) {
         // probe query q = probe . Wq + bq: one row shared by every image,
