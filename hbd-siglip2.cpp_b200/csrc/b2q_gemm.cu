@@ -611,9 +611,21 @@ static b2q_status dispatch_bn(const GemmArgs& a, cudaStream_t s, int bn) {
     return bn == 256 ? run_gemm<kOps, 256, false>(a, s) : run_gemm<kOps, 128, false>(a, s);
 }
 
+// Tile width when not forced by B2Q_TUNE_GEMM_BN: whichever of 256 and 128
+// columns finishes the persistent grid's tile rounds sooner, with a
+// 128-column tile costing about 0.6 of a 256-column one (it carries the same
+// per-K-block synchronisation for half the columns).  Large M keeps 256;
+// small M (few tiles, or a last round that is mostly empty) takes 128.
+static int auto_bn(int64_t M, int64_t N, int num_sms) {
+    const int64_t mt = (M + 127) / 128;
+    const int64_t r256 = (mt * ((N + 255) / 256) + num_sms - 1) / num_sms;
+    const int64_t r128 = (mt * ((N + 127) / 128) + num_sms - 1) / num_sms;
+    return 0.6 * static_cast<double>(r128) < 0.95 * static_cast<double>(r256) ? 128 : 256;
+}
+
 b2q_status launch_gemm(const GemmArgs& a, cudaStream_t s) {
     DeviceState* ds = state();
-    const int bn = ds->gemm_bn == 128 ? 128 : 256;
+    const int bn = ds->gemm_bn == 128 ? 128 : ds->gemm_bn == 256 ? 256 : auto_bn(a.M, a.w->N, ds->num_sms);
     return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, bn) : dispatch_bn<kOpsI8>(a, s, bn);
 }
 
