@@ -175,9 +175,10 @@ def reference_arm(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> fp32",
-        "data": "synthetic", "config": {"workload": "config-4 NaFlex vision tower (CPU sample)",
-                                        "model": "SigLIP2-so400m-patch16 vision, Q8_0", "sample": sample},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": "config-4 NaFlex batch through the 27-layer Q8_0 SigLIP2-so400m vision tower "
+                               "(CPU sample)", "sample": sample},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -484,10 +485,11 @@ def main():
         line = {
             "metric": METRIC, "value": images / (ms * 1e-3), "unit": "images/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> fp32 (Q8_0 x q8_1)",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": "config-4: 512 NaFlex images (256-1024 patches, random grids), PROBE pooling",
-                       "model": "SigLIP2-so400m-patch16 vision tower, Q8_0 (27 layers, width 1152)",
+            "config": {"workload": "config-4: 512 NaFlex images (256-1024 patches, random grids) through the "
+                                   "27-layer Q8_0 SigLIP2-so400m vision tower, PROBE pooling",
+                       "arithmetic": "Q8_0 x q8_1 int8 block dots, fp32 scales and accumulation",
                        "global_batch": args.images, "tokens_per_step": total_tokens,
                        "parallelism": f"image-sharded replicas x{world} + NCCL all-gather",
                        "l2": "inputs and activations larger than L2 (no flush)"},
