@@ -37,6 +37,7 @@ sys.path.insert(0, str(ROOT / "hbd-siglip2.cpp_b200"))
 
 METRIC = "Q8_0 vision images/s at 1/2/4/8 B200; MMQ GEMM int8 TOPS vs peak"
 N_IMAGES = 512
+CPU_SIDE = 25        # CPU samples: one 25x25-patch image, nearest square to the batch's mean patch count
 PATCH_DIM = 768
 # DRAM bytes per token of one fc1 launch: dram__bytes_read + dram__bytes_write
 # = 171.15 + 548.74 MB from one ncu capture (one pass) of
@@ -143,7 +144,7 @@ class ClockSampler:
 
 
 def cpu_tower_sample(threads=None):
-    """Time the CPU restatement of the tower on one 16x16-patch image (256
+    """Time the CPU restatement of the tower on one 25x25-patch image (625
     tokens), PROBE pooling, all host threads."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
@@ -152,7 +153,7 @@ def cpu_tower_sample(threads=None):
     n = threads or os.cpu_count() or 1
     O.set_threads(n)
     ck = synth.vision_checkpoint(synth.TowerConfig(), seed=0)
-    x = synth.patches(256, PATCH_DIM, seed=1)
+    x = synth.patches(CPU_SIDE * CPU_SIDE, PATCH_DIM, seed=1)
     O.vision_encode(ck, x[:16], 4, 4, pooling=1)   # warm the library and threads
     return O, ck, x, n
 
@@ -165,13 +166,14 @@ def reference_arm(args):
     times = []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        O.vision_encode(ck, x, 16, 16, pooling=1)
+        O.vision_encode(ck, x, CPU_SIDE, CPU_SIDE, pooling=1)
         dt = time.perf_counter() - t0
         if i >= args.warmup:
             times.append(dt)
     total = sum(times)
     value = args.steps / total
-    sample = "1 image of 16x16 = 256 patches per step (of the 512-image config-4 batch), PROBE pooling"
+    sample = (f"1 image of {CPU_SIDE}x{CPU_SIDE} = {CPU_SIDE * CPU_SIDE} patches per step (the 512-image "
+              "config-4 batch averages 613 patches per image), PROBE pooling")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
@@ -475,10 +477,11 @@ def main():
         if world == 1 and not args.no_cpu_baseline:
             O, ck_cpu, x, cores = cpu_tower_sample()
             t = time.perf_counter()
-            O.vision_encode(ck_cpu, x, 16, 16, pooling=1)
+            O.vision_encode(ck_cpu, x, CPU_SIDE, CPU_SIDE, pooling=1)
             dt = time.perf_counter() - t
             cpu = {"value": 1.0 / dt, "unit": "images/s", "cores": cores, "kind": "port",
-                   "sample": "1 image of 16x16 = 256 patches, PROBE pooling, CPU restatement (oracle/), "
+                   "sample": f"1 image of {CPU_SIDE}x{CPU_SIDE} patches (the batch averages 613), PROBE pooling, "
+                             "CPU restatement (oracle/), "
                              "OpenMP over all host threads"}
         images = args.images * args.steps
         traffic = (FC1_DRAM_BYTES_PER_TOKEN * M) if FC1_DRAM_BYTES_PER_TOKEN else None
