@@ -9,13 +9,20 @@
 // projection's quantizer reads.  Softmax in fp32 with scale 1/sqrt(72); K and
 // V are fp16 as in the reference (siglip2_vision.cpp:164-165).
 //
-// One CTA = 64 query rows of one head of one sequence (4 warps x 16 rows),
-// streaming that sequence's keys in 64-row tiles (double-buffered cp.async),
-// online softmax (FlashAttention-2 form) on mma.sync m16n8k16 tensor-core
-// fragments.  Every image of a batch is its own sequence, so no padding or
-// masking across images is needed; keys past a sequence's end are masked.
+// The default kernel (attention_tc_kernel) is built on the fifth-generation
+// tensor cores: one CTA = 128 query rows of one head of one sequence, one
+// thread per query row and TMEM lane.  Per 64-key tile, S = Q K^T goes to TMEM
+// (tcgen05.mma, kind::f16), each thread runs the online softmax on its own row
+// in registers, writes its probabilities to shared memory as the A operand of
+// P V, and adds the P V tile (TMEM) into its fp32 output registers.  The
+// score MMA of the next tile and the P V MMA of this one overlap the softmax.
+// A second kernel (attention_kernel: 64-row halves of a tile, mma.sync
+// m16n8k16 fragments, FlashAttention-2 form) and the exact checker kernel
+// stay selectable.  Every image of a batch is its own sequence, so no padding
+// or masking across images is needed; keys past a sequence's end are masked.
 #include "b2q_internal.h"
 #include "b2q_numerics.cuh"
+#include "b2q_ptx.cuh"
 
 #include <cuda_fp16.h>
 
@@ -24,19 +31,29 @@ namespace b2q {
 namespace {
 
 constexpr int kDH = 72;           // head dim
+constexpr int kTileRows = 128;    // query rows per tile-table entry
 constexpr int kRowH = 88;         // smem row stride in halves (176 B: conflict-free ldmatrix)
-constexpr int kQT = 64;           // query rows per CTA
+constexpr int kQT = 64;           // query rows per CTA of the 64-row kernels (half a tile)
 constexpr int kKT = 64;           // key rows per tile
 constexpr int kWarps = 4;
 
 struct AttnTile {
     int q_row0;     // first query row (in Q's row space)
-    int q_rows;     // valid query rows in this tile (<= 64)
+    int q_rows;     // valid query rows in this tile (<= 128)
     int k_row0;     // first key row of the sequence
     int k_len;      // keys in the sequence
     int o_row0;     // output row of the tile's first query
     int pad[3];
 };
+
+// The 64-row kernels run each 128-row table entry as two CTAs: half h covers
+// query rows 64h .. 64h + 63 of the entry (none when the entry is shorter).
+__device__ __forceinline__ AttnTile half_tile(AttnTile t, int h) {
+    t.q_row0 += kQT * h;
+    t.o_row0 += kQT * h;
+    t.q_rows = min(kQT, t.q_rows - kQT * h);
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -103,7 +120,8 @@ attention_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __rest
     __half* sK[2] = {sQ + kQT * kRowH, sQ + (kQT + kKT) * kRowH};
     __half* sV[2] = {sQ + (kQT + 2 * kKT) * kRowH, sQ + (kQT + 3 * kKT) * kRowH};
 
-    const AttnTile t = tiles[blockIdx.x];
+    const AttnTile t = half_tile(tiles[blockIdx.x >> 1], blockIdx.x & 1);
+    if (t.q_rows <= 0) return;
     const int head = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const __half* qh = q + static_cast<int64_t>(t.q_row0) * ldq + head * kDH;
@@ -268,7 +286,8 @@ attention_exact_kernel(const __half* __restrict__ q, int64_t ldq, const __half* 
                        float* __restrict__ out, int64_t ldo, float scale) {
     __shared__ float sK[kExactKeys * kDH];
     __shared__ float sV[kExactKeys * kDH];
-    const AttnTile t = tiles[blockIdx.x];
+    const AttnTile t = half_tile(tiles[blockIdx.x >> 1], blockIdx.x & 1);
+    if (t.q_rows <= 0) return;
     const int head = blockIdx.y;
     const int r = threadIdx.x;
     const bool active = r < t.q_rows;
@@ -320,6 +339,350 @@ attention_exact_kernel(const __half* __restrict__ q, int64_t ldq, const __half* 
     }
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 kernel.  Shared memory (from a 1024-byte aligned base), every
+// operand K-major with the 128-byte swizzle (row r at r * 128 bytes, its
+// 16-byte chunk c stored at chunk c ^ (r % 8)), written by the threads
+// themselves:
+//   Q      [2 K-atoms][128 rows][128 B]  dims 0..63 | 64..79 (72..79 zero)
+//   K[2]   [2 K-atoms][ 64 rows][128 B]  two key tiles in flight
+//   V^T    [80 rows (dims)][128 B = 64 keys]   rows 72..79 zero
+//   P_hi   [128 rows][128 B = 64 keys]   fp16 probabilities
+//   P_lo   [128 rows][128 B]             fp16 of their rounding remainders
+// TMEM (256 columns): S for two key tiles at columns 0 and 64, the P V tile
+// (80 columns) at column 128.
+constexpr int kTcThreads = 128;
+constexpr uint32_t kTcQ = 0, kTcK = 32768, kTcKBuf = 16384, kTcV = 65536, kTcPH = 75776, kTcPL = 92160;
+constexpr uint32_t kTcBar = 108544;
+constexpr int kTcSmem = static_cast<int>(kTcBar) + 64 + 1024;
+constexpr uint32_t kTcTmemCols = 256, kTcColO = 128;
+
+__device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
+    return row * 128u + (((chunk ^ row) & 7u) << 4);
+}
+__device__ __forceinline__ void sts_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ void sts_b32(uint32_t a, uint32_t x) {
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(x) : "memory");
+}
+__device__ __forceinline__ void cp_async16_at(uint32_t dst, const void* gmem, bool valid) {
+    const int bytes = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(gmem), "r"(bytes) : "memory");
+}
+// Writes of the generic proxy (st.shared, completed cp.async) become visible
+// to the tensor core's reads after this fence and a barrier.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Rows [0, valid) of a 72-wide fp16 operand (row stride ld halves) into a
+// K-major region of `rows` rows: chunks 0..7 (dims 0..63) in K-atom 0,
+// chunk 8 (dims 64..71) as chunk 0 of K-atom 1.  Rows >= valid are zeros.
+__device__ __forceinline__ void tc_load_rows(uint32_t region, int rows, const __half* src, int64_t ld, int valid) {
+    const uint32_t atom1 = region + static_cast<uint32_t>(rows) * 128u;
+    for (int i = threadIdx.x; i < rows * 9; i += kTcThreads) {
+        const int r = i / 9, c = i - 9 * r;
+        const bool ok = r < valid;
+        const __half* g = ok ? src + static_cast<int64_t>(r) * ld + c * 8 : src;
+        cp_async16_at(c < 8 ? region + sw128(r, c) : atom1 + sw128(r, 0), g, ok);
+    }
+}
+
+// A key tile of V in registers on its way to V^T: item i = tid + 128 it
+// (i < 288) is the pair of keys 2j, 2j+1 (j = i % 32) at dims 8c .. 8c+7
+// (c = i / 32).  Keys >= valid are zeros (their probabilities are 0, and
+// 0 x garbage could be NaN).
+struct VStage {
+    uint4 a[3], b[3];
+};
+__device__ __forceinline__ void tc_fetch_v(VStage& st, const __half* src, int64_t ld, int valid) {
+#pragma unroll
+    for (int it = 0; it < 3; ++it) {
+        const int i = threadIdx.x + kTcThreads * it;
+        st.a[it] = st.b[it] = make_uint4(0, 0, 0, 0);
+        if (i < 288) {
+            const int c = i >> 5, j = i & 31;
+            if (2 * j < valid) st.a[it] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(2 * j) * ld + 8 * c));
+            if (2 * j + 1 < valid)
+                st.b[it] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(2 * j + 1) * ld + 8 * c));
+        }
+    }
+}
+// V^T row d = 8c + e holds keys 2j, 2j+1 in the 32-bit word at byte 4j:
+// chunk j / 4 (swizzled by d % 8 = e), word j % 4.  One warp stores one row's
+// 32 words per instruction: all 32 banks, no conflicts.
+__device__ __forceinline__ void tc_store_vt(const VStage& st, uint32_t vt) {
+#pragma unroll
+    for (int it = 0; it < 3; ++it) {
+        const int i = threadIdx.x + kTcThreads * it;
+        if (i < 288) {
+            const uint32_t c = i >> 5, j = i & 31;
+            const uint32_t aw[4] = {st.a[it].x, st.a[it].y, st.a[it].z, st.a[it].w};
+            const uint32_t bw[4] = {st.b[it].x, st.b[it].y, st.b[it].z, st.b[it].w};
+#pragma unroll
+            for (uint32_t e = 0; e < 8; ++e) {
+                const uint32_t word = __byte_perm(aw[e >> 1], bw[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
+                sts_b32(vt + (8 * c + e) * 128u + ((((j >> 2) ^ e) & 7u) << 4) + 4u * (j & 3u), word);
+            }
+        }
+    }
+}
+
+// S(128 x 64) = Q K^T over the 80 padded dims: four K = 16 steps inside
+// K-atom 0 (start address + 32 bytes each) and one in K-atom 1.
+__device__ __forceinline__ void tc_issue_scores(uint32_t tmem_s, uint32_t q, uint32_t k) {
+    constexpr uint32_t idesc = idesc_f16_f32(128, 64);
+#pragma unroll
+    for (uint32_t ks = 0; ks < 5; ++ks) {
+        const uint32_t qa = ks < 4 ? q + 32u * ks : q + 128u * 128u;
+        const uint32_t kb = ks < 4 ? k + 32u * ks : k + 64u * 128u;
+        mma_f16(tmem_s, smem_desc_k_sw128(qa), smem_desc_k_sw128(kb), idesc, ks > 0 ? 1u : 0u);
+    }
+}
+// O_tile(128 x 80) = P_hi V + P_lo V over the tile's 64 keys.
+__device__ __forceinline__ void tc_issue_pv(uint32_t tmem_o, uint32_t ph, uint32_t pl, uint32_t vt) {
+    constexpr uint32_t idesc = idesc_f16_f32(128, 80);
+#pragma unroll
+    for (uint32_t ks = 0; ks < 4; ++ks)
+        mma_f16(tmem_o, smem_desc_k_sw128(ph + 32u * ks), smem_desc_k_sw128(vt + 32u * ks), idesc, ks > 0 ? 1u : 0u);
+#pragma unroll
+    for (uint32_t ks = 0; ks < 4; ++ks)
+        mma_f16(tmem_o, smem_desc_k_sw128(pl + 32u * ks), smem_desc_k_sw128(vt + 32u * ks), idesc, 1u);
+}
+
+__device__ __forceinline__ void tc_raise(uint32_t* err, volatile uint32_t* abort_flag, uint32_t code) {
+    *abort_flag = 1u;
+    atomicCAS(err, 0u, code);
+}
+
+// Per key tile kt (b = kt % 2), with two block barriers:
+//   [A] K tile kt+1 has landed and every thread has read S(kt-1):
+//       thread 0 issues S(kt+1) into TMEM buffer b^1.
+//   [B] wait for S(kt), read it, start loading K tile kt+2 into K buffer b,
+//       online softmax on the thread's row.
+//   [C] wait for P V of tile kt-1 (which frees P and V^T), add it to the
+//       output registers, rescale them to this tile's running max.
+//   [D] V tile kt (already in registers) to V^T; fetch V tile kt+1.
+//   [E] probabilities to P_hi / P_lo.
+//   [F] thread 0 issues P V for tile kt.
+// Every wait is bounded; an expired wait records its code, and the block
+// leaves the loop together at the next barrier.
+__global__ void __launch_bounds__(kTcThreads, 2)
+attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __restrict__ k, int64_t ldk,
+                    const __half* __restrict__ v, int64_t ldv, const AttnTile* __restrict__ tiles,
+                    float* __restrict__ out, int64_t ldo, float scale_log2, uint32_t* err, uint64_t timeout_ns,
+                    int stall) {
+    extern __shared__ __align__(1024) uint8_t tc_smem[];
+    const uint32_t raw = smem_u32(tc_smem);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    const uint32_t sQ = base + kTcQ, sK = base + kTcK, sV = base + kTcV, sPH = base + kTcPH, sPL = base + kTcPL;
+    const uint32_t bar_s0 = base + kTcBar, bar_s1 = bar_s0 + 8, bar_o = bar_s0 + 16, bar_fin = bar_s0 + 24;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + (base - raw) + kTcBar + 32);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const AttnTile t = tiles[blockIdx.x];
+    const int head = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const __half* qh = q + static_cast<int64_t>(t.q_row0) * ldq + head * kDH;
+    const __half* kh = k + static_cast<int64_t>(t.k_row0) * ldk + head * kDH;
+    const __half* vh = v + static_cast<int64_t>(t.k_row0) * ldv + head * kDH;
+    const int n_kt = (t.k_len + kKT - 1) / kKT;
+
+    if (tid == 0) {
+        mbar_init(bar_s0, 1);
+        mbar_init(bar_s1, 1);
+        mbar_init(bar_o, 1);
+        mbar_init(bar_fin, 1);
+        *abort_flag = 0u;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, kTcTmemCols);
+        tc_fence_before();
+    }
+    // zero padding: dims 72..79 (chunk 1 of K-atom 1) of Q and both K buffers,
+    // V^T rows 72..79
+    for (int r = tid; r < 128; r += kTcThreads) sts_v4(sQ + 128u * 128u + sw128(r, 1), 0, 0, 0, 0);
+    for (int i = tid; i < 128; i += kTcThreads) {
+        const uint32_t r = i & 63, b = i >> 6;
+        sts_v4(sK + b * kTcKBuf + 64u * 128u + sw128(r, 1), 0, 0, 0, 0);
+    }
+    for (int i = tid; i < 64; i += kTcThreads) sts_v4(sV + (72u + (i >> 3)) * 128u + 16u * (i & 7), 0, 0, 0, 0);
+
+    tc_load_rows(sQ, 128, qh, ldq, t.q_rows);
+    tc_load_rows(sK, 64, kh, ldk, min(kKT, t.k_len));
+    cp_async_commit();
+    VStage vs;
+    tc_fetch_v(vs, vh, ldv, min(kKT, t.k_len));
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    if (tid == 0 && !stall) {
+        tc_issue_scores(tmem, sQ, sK);
+        mma_commit(bar_s0);
+    }
+    if (n_kt > 1) {
+        tc_load_rows(sK + kTcKBuf, 64, kh + static_cast<int64_t>(kKT) * ldk, ldk, min(kKT, t.k_len - kKT));
+        cp_async_commit();
+    }
+
+    float o[kDH];
+#pragma unroll
+    for (int d = 0; d < kDH; ++d) o[d] = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool failed = false, finished = false;
+
+    for (int kt = 0; kt < n_kt; ++kt) {
+        const uint32_t b = kt & 1;
+        // [A]
+        cp_async_wait<0>();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        if (__syncthreads_or(failed)) break;
+        tc_fence_after();
+        if (tid == 0 && !stall && kt + 1 < n_kt) {
+            tc_issue_scores(tmem + 64u * (b ^ 1u), sQ, sK + kTcKBuf * (b ^ 1u));
+            mma_commit(b ? bar_s0 : bar_s1);
+        }
+        // [B]
+        if (!mbar_wait(b ? bar_s1 : bar_s0, (kt >> 1) & 1, abort_flag, timeout_ns)) {
+            tc_raise(err, abort_flag, kDevTimeoutTmemFull);
+            failed = true;
+        }
+        tc_fence_after();
+        float s[64];
+        {
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + 64u * b, r0);
+            tmem_ld_32x32b_x32(tmem + lane_base + 64u * b + 32u, r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                s[i] = __uint_as_float(r0[i]);
+                s[32 + i] = __uint_as_float(r1[i]);
+            }
+        }
+        if (kt + 2 < n_kt) {
+            const int k0 = (kt + 2) * kKT;
+            tc_load_rows(sK + kTcKBuf * b, 64, kh + static_cast<int64_t>(k0) * ldk, ldk, min(kKT, t.k_len - k0));
+            cp_async_commit();
+        }
+        const int valid = t.k_len - kt * kKT;   // keys of this tile that exist (>= 1)
+        float mx = m_run;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            float x = s[i] * scale_log2;
+            if (i >= valid) x = -INFINITY;
+            s[i] = x;
+            mx = fmaxf(mx, x);
+        }
+        const float corr = exp2f(m_run - mx);
+        float rowsum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            s[i] = exp2f(s[i] - mx);
+            rowsum += s[i];
+        }
+        l_run = l_run * corr + rowsum;
+        m_run = mx;
+        // [C]
+        if (kt > 0) {
+            if (!mbar_wait(bar_o, (kt - 1) & 1, abort_flag, timeout_ns)) {
+                tc_raise(err, abort_flag, kDevTimeoutTmemFull);
+                failed = true;
+            }
+            tc_fence_after();
+            uint32_t r0[32], r1[32], r2[16];
+            tmem_ld_32x32b_x32(tmem + lane_base + kTcColO, r0);
+            tmem_ld_32x32b_x32(tmem + lane_base + kTcColO + 32u, r1);
+            tmem_ld_32x32b_x16(tmem + lane_base + kTcColO + 64u, r2);
+            tmem_ld_wait();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) {
+                o[d] = (o[d] + __uint_as_float(r0[d])) * corr;
+                o[32 + d] = (o[32 + d] + __uint_as_float(r1[d])) * corr;
+            }
+#pragma unroll
+            for (int d = 0; d < 8; ++d) o[64 + d] = (o[64 + d] + __uint_as_float(r2[d])) * corr;
+        }
+        // [D]
+        tc_store_vt(vs, sV);
+        if (kt + 1 < n_kt) {
+            const int k0 = (kt + 1) * kKT;
+            tc_fetch_v(vs, vh + static_cast<int64_t>(k0) * ldv, ldv, min(kKT, t.k_len - k0));
+        }
+        // [E] row tid of P: keys 8c .. 8c+7 in chunk c
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) split_half2(s[8 * c + 2 * e], s[8 * c + 2 * e + 1], hi[e], lo[e]);
+            sts_v4(sPH + sw128(tid, c), hi[0], hi[1], hi[2], hi[3]);
+            sts_v4(sPL + sw128(tid, c), lo[0], lo[1], lo[2], lo[3]);
+        }
+        // [F]
+        fence_proxy_async_smem();
+        tc_fence_before();
+        if (__syncthreads_or(failed)) break;
+        tc_fence_after();
+        if (tid == 0 && !stall) {
+            tc_issue_pv(tmem + kTcColO, sPH, sPL, sV);
+            mma_commit(bar_o);
+        }
+        finished = kt + 1 == n_kt;
+    }
+
+    if (finished) {
+        if (!mbar_wait(bar_o, (n_kt - 1) & 1, abort_flag, timeout_ns)) {
+            tc_raise(err, abort_flag, kDevTimeoutTmemFull);
+            failed = true;
+        }
+        tc_fence_after();
+        uint32_t r0[32], r1[32], r2[16];
+        tmem_ld_32x32b_x32(tmem + lane_base + kTcColO, r0);
+        tmem_ld_32x32b_x32(tmem + lane_base + kTcColO + 32u, r1);
+        tmem_ld_32x32b_x16(tmem + lane_base + kTcColO + 64u, r2);
+        tmem_ld_wait();
+#pragma unroll
+        for (int d = 0; d < 32; ++d) {
+            o[d] += __uint_as_float(r0[d]);
+            o[32 + d] += __uint_as_float(r1[d]);
+        }
+#pragma unroll
+        for (int d = 0; d < 8; ++d) o[64 + d] += __uint_as_float(r2[d]);
+        if (!failed && tid < t.q_rows) {
+            const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+            float* dst = out + static_cast<int64_t>(t.o_row0 + tid) * ldo + head * kDH;
+#pragma unroll
+            for (int d = 0; d < kDH; d += 2)
+                *reinterpret_cast<float2*>(dst + d) = make_float2(o[d] * inv, o[d + 1] * inv);
+        }
+    }
+
+    // Release: no copy in flight into shared memory, every MMA this CTA
+    // issued retired (the commit below arrives once they all have), every
+    // TMEM load landed.
+    cp_async_wait<0>();
+    tmem_ld_wait();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        tc_fence_after();
+        mma_commit(bar_fin);
+        volatile uint32_t no_abort = 0;
+        mbar_wait(bar_fin, 0, &no_abort, 100000000ull);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTcTmemCols);
+    }
+}
+
 }  // namespace
 
 size_t attn_tiles_bytes(int n_tiles) { return static_cast<size_t>(n_tiles) * sizeof(AttnTile); }
@@ -333,10 +696,10 @@ int attn_build_tiles(const int* q_off, const int* q_len, const int* k_off, const
     AttnTile* t = static_cast<AttnTile*>(tiles);
     int n = 0;
     for (int s = 0; s < n_seq; ++s) {
-        for (int q0 = 0; q0 < q_len[s]; q0 += kQT) {
+        for (int q0 = 0; q0 < q_len[s]; q0 += kTileRows) {
             if (n >= max_tiles) return -1;
             t[n].q_row0 = q_off[s] + q0;
-            t[n].q_rows = q_len[s] - q0 < kQT ? q_len[s] - q0 : kQT;
+            t[n].q_rows = q_len[s] - q0 < kTileRows ? q_len[s] - q0 : kTileRows;
             t[n].k_row0 = k_off[s];
             t[n].k_len = k_len[s];
             t[n].o_row0 = o_off[s] + q0;
@@ -352,12 +715,26 @@ cudaError_t launch_attention(const __half* q, int64_t ldq, const __half* k, int6
                              cudaStream_t s, bool force_exact) {
     if (n_tiles <= 0) return cudaSuccess;
     DeviceState* ds = state();
+    const AttnTile* tiles = static_cast<const AttnTile*>(tiles_dev);
     if (force_exact || (ds && ds->attn_exact)) {
         const float scale = 1.0f / sqrtf(static_cast<float>(kDH));
+        dim3 grid(static_cast<unsigned>(2 * n_tiles), static_cast<unsigned>(n_head));
+        attention_exact_kernel<<<grid, kExactThreads, 0, s>>>(q, ldq, k, ldk, v, ldv, tiles, out, ldo, scale);
+        count_launch();
+        return cudaGetLastError();
+    }
+    const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kDH));
+    if (ds && ds->attn_kernel == 0) {
+        static bool tc_configured = false;
+        if (!tc_configured) {
+            cudaError_t e =
+                cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+            if (e != cudaSuccess) return e;
+            tc_configured = true;
+        }
         dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_head));
-        attention_exact_kernel<<<grid, kExactThreads, 0, s>>>(q, ldq, k, ldk, v, ldv,
-                                                              static_cast<const AttnTile*>(tiles_dev), out, ldo,
-                                                              scale);
+        attention_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(q, ldq, k, ldk, v, ldv, tiles, out, ldo, scale_log2,
+                                                             ds->err, ds->timeout_ns, ds->test_stall);
         count_launch();
         return cudaGetLastError();
     }
@@ -368,10 +745,8 @@ cudaError_t launch_attention(const __half* q, int64_t ldq, const __half* k, int6
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(kDH));
-    dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(n_head));
-    attention_kernel<<<grid, kWarps * 32, smem, s>>>(q, ldq, k, ldk, v, ldv, static_cast<const AttnTile*>(tiles_dev),
-                                                  out, ldo, scale_log2);
+    dim3 grid(static_cast<unsigned>(2 * n_tiles), static_cast<unsigned>(n_head));
+    attention_kernel<<<grid, kWarps * 32, smem, s>>>(q, ldq, k, ldk, v, ldv, tiles, out, ldo, scale_log2);
     count_launch();
     return cudaGetLastError();
 }

@@ -120,6 +120,10 @@ b2q_status b2q_tune(int key, int64_t value) {
         case B2Q_TUNE_TEST_STALL:
             ds->test_stall = value ? 1 : 0;
             return B2Q_OK;
+        case B2Q_TUNE_ATTN_KERNEL:
+            if (value != 0 && value != 1) return set_error(B2Q_ERR_INVALID, "attention kernel must be 0 or 1");
+            ds->attn_kernel = static_cast<int>(value);
+            return B2Q_OK;
         default:
             return set_error(B2Q_ERR_INVALID, "unknown tuning key");
     }
@@ -339,7 +343,7 @@ b2q_status b2q_block_sums(const b2q_weight* w, const void* act, int64_t M, int32
 size_t b2q_attention_scratch_bytes(const int32_t* q_len, int32_t n_seq) {
     if (!q_len || n_seq <= 0) return 0;
     int64_t tiles = 0;
-    for (int32_t s = 0; s < n_seq; ++s) tiles += (q_len[s] + 63) / 64;
+    for (int32_t s = 0; s < n_seq; ++s) tiles += (q_len[s] + 127) / 128;
     return attn_tiles_bytes(static_cast<int>(tiles));
 }
 

@@ -37,7 +37,8 @@ struct DeviceState {
     uint64_t timeout_ns = 2000000000ull;
     int gemm_bn = 0;              // GEMM tile width: 128, 256, or 0 = by shape
     int attn_exact = 0;           // attention in the checker's fixed fp32 order
-    int test_stall = 0;           // GEMM producer issues no loads (failure-path tests)
+    int attn_kernel = 0;          // 0 = tcgen05 kernel, 1 = mma.sync kernel
+    int test_stall = 0;           // GEMM producer / attention MMA issuer idle (failure-path tests)
 };
 DeviceState* state();             // per-thread current device state
 void count_launch();              // every kernel launch of the library counts once

@@ -62,11 +62,21 @@ b2q_status b2q_init(int device, int ops_mode);
  *   B2Q_TUNE_TIMEOUT_NS: bound of every in-kernel wait (default 2 s)
  *   B2Q_TUNE_ATTN_EXACT: 1 = attention in one fixed fp32 order (slow; makes
  *                        the tower bit-reproducible), 0 = tensor cores
- *   B2Q_TUNE_TEST_STALL: 1 = (tests only) the GEMM's TMA producer issues
- *                        nothing, so the other roles' bounded waits expire
- *                        and the launch reports B2Q_ERR_DEVICE through
- *                        b2q_check_device without faulting or hanging */
-enum { B2Q_TUNE_GEMM_BN = 1, B2Q_TUNE_TIMEOUT_NS = 2, B2Q_TUNE_ATTN_EXACT = 3, B2Q_TUNE_TEST_STALL = 4 };
+ *   B2Q_TUNE_TEST_STALL: 1 = (tests only) the GEMM's TMA producer and the
+ *                        attention's MMA issuer issue nothing, so the other
+ *                        roles' bounded waits expire and the launch reports
+ *                        B2Q_ERR_DEVICE through b2q_check_device without
+ *                        faulting or hanging
+ *   B2Q_TUNE_ATTN_KERNEL: tensor-core attention kernel: 0 = tcgen05 (TMEM
+ *                        accumulators, 128 queries per CTA; default),
+ *                        1 = mma.sync (64 queries per CTA) */
+enum {
+    B2Q_TUNE_GEMM_BN = 1,
+    B2Q_TUNE_TIMEOUT_NS = 2,
+    B2Q_TUNE_ATTN_EXACT = 3,
+    B2Q_TUNE_TEST_STALL = 4,
+    B2Q_TUNE_ATTN_KERNEL = 5
+};
 b2q_status b2q_tune(int key, int64_t value);
 /* Reads (and clears) the device error word after synchronising `stream`;
  * B2Q_ERR_DEVICE when it was set: codes 1-4 = an in-kernel wait expired

@@ -25,6 +25,14 @@ def dev():
     b2q.init(0)
 
 
+@pytest.fixture(params=[0, 1], ids=["tcgen05", "mma_sync"])
+def kernel(request, dev):
+    """Both tensor-core kernels (B2Q_TUNE_ATTN_KERNEL) meet the same bar."""
+    b2q.tune(b2q.TUNE_ATTN_KERNEL, request.param)
+    yield request.param
+    b2q.tune(b2q.TUNE_ATTN_KERNEL, 0)
+
+
 def check_close(out, ref):
     err = np.abs(out - ref).max()
     cos = (out * ref).sum(1) / (np.linalg.norm(out, axis=1) * np.linalg.norm(ref, axis=1) + 1e-30)
@@ -32,8 +40,8 @@ def check_close(out, ref):
     assert cos.min() >= 0.99999, cos.min()
 
 
-@pytest.mark.parametrize("lens", [[1], [7], [64, 65], [729], [1, 5, 100, 256, 1024]])
-def test_self_attention_varlen(oracle, dev, lens):
+@pytest.mark.parametrize("lens", [[1], [7], [64, 65], [127, 128, 129], [729], [1, 5, 100, 256, 1024]])
+def test_self_attention_varlen(oracle, kernel, lens):
     rng = np.random.default_rng(len(lens) * 1000 + sum(lens))
     T = sum(lens)
     qkv = rng.standard_normal((T, 3 * H)).astype(np.float32)
@@ -47,7 +55,23 @@ def test_self_attention_varlen(oracle, dev, lens):
     check_close(out.cpu().numpy(), ref)
 
 
-def test_probe_query_shared_row(oracle, dev):
+def test_large_logits(oracle, kernel):
+    # scores spanning hundreds of units: the running max moves between key
+    # tiles and most probabilities underflow
+    rng = np.random.default_rng(11)
+    lens = [300, 77]
+    T = sum(lens)
+    qkv = (rng.standard_normal((T, 3 * H)) * np.r_[np.full(H, 4.0), np.full(H, 4.0), np.ones(H)]).astype(np.float16)
+    ref = oracle.attention(qkv.astype(np.float32), NH, lens)
+    offs = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    t = torch.from_numpy(qkv).cuda()
+    out = torch.full((T, H), float("nan"), dtype=torch.float32, device="cuda")
+    b2q.attention(t, 3 * H, t[:, H:], 3 * H, t[:, 2 * H:], 3 * H, offs, lens, offs, lens, offs, NH, out, H)
+    torch.cuda.synchronize()
+    check_close(out.cpu().numpy(), ref)
+
+
+def test_probe_query_shared_row(oracle, kernel):
     # attention-pool head: one probe query (shared by every image) against each image's keys
     rng = np.random.default_rng(7)
     lens = [729, 300, 1]
