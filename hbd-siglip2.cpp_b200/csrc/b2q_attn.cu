@@ -344,17 +344,18 @@ attention_exact_kernel(const __half* __restrict__ q, int64_t ldq, const __half* 
 // operand K-major with the 128-byte swizzle (row r at r * 128 bytes, its
 // 16-byte chunk c stored at chunk c ^ (r % 8)), written by the threads
 // themselves:
-//   Q      [2 K-atoms][128 rows][128 B]  dims 0..63 | 64..79 (72..79 zero)
-//   K[2]   [2 K-atoms][ 64 rows][128 B]  two key tiles in flight
-//   V^T    [80 rows (dims)][128 B = 64 keys]   rows 72..79 zero
-//   P_hi   [128 rows][128 B = 64 keys]   fp16 probabilities
-//   P_lo   [128 rows][128 B]             fp16 of their rounding remainders
-// TMEM (256 columns): S for two key tiles at columns 0 and 64, the P V tile
-// (80 columns) at column 128.
-constexpr int kTcThreads = 128;
-constexpr uint32_t kTcQ = 0, kTcK = 32768, kTcKBuf = 16384, kTcV = 65536, kTcPH = 75776, kTcPL = 92160;
-constexpr uint32_t kTcBar = 108544;
-constexpr int kTcSmem = static_cast<int>(kTcBar) + 64 + 1024;
+//   Q       [2 K-atoms][128 rows][128 B]  dims 0..63 | 64..79 (72..79 zero)
+//   K[2]    [2 K-atoms][ 64 rows][128 B]  key tiles j % 2
+//   V^T[2]  [80 rows (dims)][128 B = 64 keys]   row 72 ones, 73..79 zero
+// TMEM (256 columns): two 64-column buffers, each holding first the scores
+// S(j) of key tile j (fp32) and then, over them, its probabilities as the A
+// operand of P V: P_hi in columns 0..31 and P_lo in 32..63 (fp16 pairs);
+// the output accumulator O (80 columns; column 72 = running row sum) at
+// column 128.
+constexpr int kTcThreads = 160;   // warps 0-3: softmax (one query row each), warp 4: loads + MMA issue
+constexpr uint32_t kTcQ = 0, kTcK = 32768, kTcKBuf = 16384, kTcV = 65536, kTcVBuf = 10240;
+constexpr uint32_t kTcBar = 86016;
+constexpr int kTcSmem = static_cast<int>(kTcBar) + 64 + 1024;   // 7 barriers, TMEM slot, abort flag
 constexpr uint32_t kTcTmemCols = 256, kTcColO = 128;
 
 __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
@@ -375,56 +376,61 @@ __device__ __forceinline__ void cp_async16_at(uint32_t dst, const void* gmem, bo
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
-// Rows [0, valid) of a 72-wide fp16 operand (row stride ld halves) into a
-// K-major region of `rows` rows: chunks 0..7 (dims 0..63) in K-atom 0,
-// chunk 8 (dims 64..71) as chunk 0 of K-atom 1.  Rows >= valid are zeros.
-__device__ __forceinline__ void tc_load_rows(uint32_t region, int rows, const __half* src, int64_t ld, int valid) {
-    const uint32_t atom1 = region + static_cast<uint32_t>(rows) * 128u;
-    for (int i = threadIdx.x; i < rows * 9; i += kTcThreads) {
-        const int r = i / 9, c = i - 9 * r;
-        const bool ok = r < valid;
-        const __half* g = ok ? src + static_cast<int64_t>(r) * ld + c * 8 : src;
-        cp_async16_at(c < 8 ? region + sw128(r, c) : atom1 + sw128(r, 0), g, ok);
+// Row r of a 72-wide fp16 operand into a K-major region of `rows` rows:
+// chunks 0..7 (dims 0..63) in K-atom 0, chunk 8 (dims 64..71) as chunk 0 of
+// K-atom 1.
+__device__ __forceinline__ uint32_t tc_chunk_addr(uint32_t region, uint32_t rows, uint32_t r, uint32_t c) {
+    return c < 8 ? region + sw128(r, c) : region + rows * 128u + sw128(r, 0);
+}
+
+// Key tile into a K buffer by the control warp: lane l copies rows l and
+// l + 32; rows >= valid are zeros.
+__device__ __forceinline__ void tc_load_k(uint32_t buf, const __half* src, int64_t ld, int valid, uint32_t lane) {
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+        const uint32_t r = lane + 32u * h;
+        const bool ok = static_cast<int>(r) < valid;
+        const __half* g = src + (ok ? static_cast<int64_t>(r) * ld : 0);
+#pragma unroll
+        for (uint32_t c = 0; c < 9; ++c) cp_async16_at(tc_chunk_addr(buf, 64, r, c), g + 8 * c, ok);
     }
 }
 
-// A key tile of V in registers on its way to V^T: item i = tid + 128 it
-// (i < 288) is the pair of keys 2j, 2j+1 (j = i % 32) at dims 8c .. 8c+7
-// (c = i / 32).  Keys >= valid are zeros (their probabilities are 0, and
-// 0 x garbage could be NaN).
+// A key tile of V in the control warp's registers on its way to V^T: lane j
+// holds keys 2j and 2j+1 (all 72 dims).  Keys >= valid are zeros (their
+// probabilities are 0, and 0 x garbage could be NaN).
 struct VStage {
-    uint4 a[3], b[3];
+    uint4 a[9], b[9];
 };
-__device__ __forceinline__ void tc_fetch_v(VStage& st, const __half* src, int64_t ld, int valid) {
+__device__ __forceinline__ void tc_fetch_v(VStage& st, const __half* src, int64_t ld, int valid, uint32_t j) {
+    const bool ok0 = static_cast<int>(2 * j) < valid, ok1 = static_cast<int>(2 * j + 1) < valid;
+    const __half* r0 = src + (ok0 ? static_cast<int64_t>(2 * j) * ld : 0);
+    const __half* r1 = src + (ok1 ? static_cast<int64_t>(2 * j + 1) * ld : 0);
 #pragma unroll
-    for (int it = 0; it < 3; ++it) {
-        const int i = threadIdx.x + kTcThreads * it;
-        st.a[it] = st.b[it] = make_uint4(0, 0, 0, 0);
-        if (i < 288) {
-            const int c = i >> 5, j = i & 31;
-            if (2 * j < valid) st.a[it] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(2 * j) * ld + 8 * c));
-            if (2 * j + 1 < valid)
-                st.b[it] = __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(2 * j + 1) * ld + 8 * c));
-        }
+    for (int c = 0; c < 9; ++c) {
+        st.a[c] = ok0 ? __ldg(reinterpret_cast<const uint4*>(r0 + 8 * c)) : make_uint4(0, 0, 0, 0);
+        st.b[c] = ok1 ? __ldg(reinterpret_cast<const uint4*>(r1 + 8 * c)) : make_uint4(0, 0, 0, 0);
     }
 }
 // V^T row d = 8c + e holds keys 2j, 2j+1 in the 32-bit word at byte 4j:
-// chunk j / 4 (swizzled by d % 8 = e), word j % 4.  One warp stores one row's
-// 32 words per instruction: all 32 banks, no conflicts.
-__device__ __forceinline__ void tc_store_vt(const VStage& st, uint32_t vt) {
+// chunk j / 4 (swizzled by d % 8 = e), word j % 4.  Each store instruction
+// writes one row's 32 words: all 32 banks, no conflicts.
+__device__ __forceinline__ void tc_store_vt(const VStage& st, uint32_t vt, uint32_t j) {
 #pragma unroll
-    for (int it = 0; it < 3; ++it) {
-        const int i = threadIdx.x + kTcThreads * it;
-        if (i < 288) {
-            const uint32_t c = i >> 5, j = i & 31;
-            const uint32_t aw[4] = {st.a[it].x, st.a[it].y, st.a[it].z, st.a[it].w};
-            const uint32_t bw[4] = {st.b[it].x, st.b[it].y, st.b[it].z, st.b[it].w};
+    for (uint32_t c = 0; c < 9; ++c) {
+        const uint32_t aw[4] = {st.a[c].x, st.a[c].y, st.a[c].z, st.a[c].w};
+        const uint32_t bw[4] = {st.b[c].x, st.b[c].y, st.b[c].z, st.b[c].w};
+        const uint32_t row0 = vt + 8u * c * 128u + 4u * (j & 3u);
 #pragma unroll
-            for (uint32_t e = 0; e < 8; ++e) {
-                const uint32_t word = __byte_perm(aw[e >> 1], bw[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
-                sts_b32(vt + (8 * c + e) * 128u + ((((j >> 2) ^ e) & 7u) << 4) + 4u * (j & 3u), word);
-            }
+        for (uint32_t e = 0; e < 8; ++e) {
+            const uint32_t word = __byte_perm(aw[e >> 1], bw[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
+            sts_b32(row0 + e * 128u + ((((j >> 2) ^ e) & 7u) << 4), word);
         }
     }
 }
@@ -440,34 +446,69 @@ __device__ __forceinline__ void tc_issue_scores(uint32_t tmem_s, uint32_t q, uin
         mma_f16(tmem_s, smem_desc_k_sw128(qa), smem_desc_k_sw128(kb), idesc, ks > 0 ? 1u : 0u);
     }
 }
-// O_tile(128 x 80) = P_hi V + P_lo V over the tile's 64 keys.
-__device__ __forceinline__ void tc_issue_pv(uint32_t tmem_o, uint32_t ph, uint32_t pl, uint32_t vt) {
+// O(128 x 80) (+)= P_hi V + P_lo V over the tile's 64 keys, P from TMEM
+// (16 keys = 8 columns per step).  Row 72 of V^T is all ones, so column 72
+// of O accumulates the row sums of P.
+__device__ __forceinline__ void tc_issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint32_t vt, bool accumulate) {
     constexpr uint32_t idesc = idesc_f16_f32(128, 80);
 #pragma unroll
     for (uint32_t ks = 0; ks < 4; ++ks)
-        mma_f16(tmem_o, smem_desc_k_sw128(ph + 32u * ks), smem_desc_k_sw128(vt + 32u * ks), idesc, ks > 0 ? 1u : 0u);
+        mma_f16_ts(tmem_o, tmem_p + 8u * ks, smem_desc_k_sw128(vt + 32u * ks), idesc,
+                   (accumulate || ks > 0) ? 1u : 0u);
 #pragma unroll
     for (uint32_t ks = 0; ks < 4; ++ks)
-        mma_f16(tmem_o, smem_desc_k_sw128(pl + 32u * ks), smem_desc_k_sw128(vt + 32u * ks), idesc, 1u);
+        mma_f16_ts(tmem_o, tmem_p + 32u + 8u * ks, smem_desc_k_sw128(vt + 32u * ks), idesc, 1u);
 }
 
-__device__ __forceinline__ void tc_raise(uint32_t* err, volatile uint32_t* abort_flag, uint32_t code) {
-    *abort_flag = 1u;
-    atomicCAS(err, 0u, code);
+// Bounded wait taken by a whole warp: the warp goes on only if every lane's
+// wait succeeded (an expiry records `code` and raises the CTA's abort flag).
+__device__ __forceinline__ bool tc_warp_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                             uint64_t timeout_ns, uint32_t* err, uint32_t code) {
+    const bool ok = mbar_wait(bar, parity, abort_flag, timeout_ns);
+    if (!ok) {
+        *abort_flag = 1u;
+        atomicCAS(err, 0u, code);
+    }
+    return __all_sync(0xffffffffu, ok);
 }
 
-// Per key tile kt (b = kt % 2), with two block barriers:
-//   [A] K tile kt+1 has landed and every thread has read S(kt-1):
-//       thread 0 issues S(kt+1) into TMEM buffer b^1.
-//   [B] wait for S(kt), read it, start loading K tile kt+2 into K buffer b,
-//       online softmax on the thread's row.
-//   [C] wait for P V of tile kt-1 (which frees P and V^T), add it to the
-//       output registers, rescale them to this tile's running max.
-//   [D] V tile kt (already in registers) to V^T; fetch V tile kt+1.
-//   [E] probabilities to P_hi / P_lo.
-//   [F] thread 0 issues P V for tile kt.
-// Every wait is bounded; an expired wait records its code, and the block
-// leaves the loop together at the next barrier.
+// Multiplies this thread's row of O (80 columns) in TMEM by f.
+__device__ __forceinline__ void tc_scale_o(uint32_t taddr, float f) {
+    uint32_t r[32], r2[16];
+#pragma unroll
+    for (uint32_t h = 0; h < 2; ++h) {
+        tmem_ld_32x32b_x32(taddr + 32u * h, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+        tmem_st_32x32b_x32(taddr + 32u * h, r);
+    }
+    tmem_ld_32x32b_x16(taddr + 64u, r2);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r2[i] = __float_as_uint(__uint_as_float(r2[i]) * f);
+    tmem_st_32x32b_x16(taddr + 64u, r2);
+    tmem_st_wait();
+}
+
+// Roles and hand-offs (mbarriers; no block-wide barrier inside the key loop).
+// Key tile j uses TMEM buffer, K buffer and V^T buffer j % 2.
+//   control warp, per key tile j:
+//     wait until the four softmax warps have written P(j); issue
+//     O (+)= P(j) V(j); once that is done (P(j) and V^T(j) read), issue
+//     S(j+2) into the same TMEM buffer (its K tile was loaded one iteration
+//     earlier) and store V tile j+2 (fetched one tile ahead into registers)
+//     to V^T; once S(j+1) has read its K buffer, load K tile j+3 into it.
+//   softmax warps (thread = query row = TMEM lane), per key tile j:
+//     wait for S(j), read the row, mask, row max, probabilities
+//     p = exp2(s * scale_log2 - m) against a reference m that moves only
+//     when the row's maximum exceeds it by more than 8 (so p <= 256, exact
+//     in the fp16 split); if m moved, wait for P(j-1) V(j-1) and rescale the
+//     row of O in TMEM; write P_hi / P_lo over S(j); signal.
+// The softmax warps never wait for a P V product in the steady state, so
+// the score tiles stream through them while the tensor core runs behind.
+// Every wait is bounded; an expired wait records its code, raises the CTA's
+// abort flag (every other wait then gives up too), and the roles unwind.
 __global__ void __launch_bounds__(kTcThreads, 2)
 attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __restrict__ k, int64_t ldk,
                     const __half* __restrict__ v, int64_t ldv, const AttnTile* __restrict__ tiles,
@@ -476,14 +517,19 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     extern __shared__ __align__(1024) uint8_t tc_smem[];
     const uint32_t raw = smem_u32(tc_smem);
     const uint32_t base = (raw + 1023u) & ~1023u;
-    const uint32_t sQ = base + kTcQ, sK = base + kTcK, sV = base + kTcV, sPH = base + kTcPH, sPL = base + kTcPL;
-    const uint32_t bar_s0 = base + kTcBar, bar_s1 = bar_s0 + 8, bar_o = bar_s0 + 16, bar_fin = bar_s0 + 24;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + (base - raw) + kTcBar + 32);
+    const uint32_t sQ = base + kTcQ, sK = base + kTcK, sV = base + kTcV;
+    // P(j) is signalled on bar_p0 + 8 * (j % 2): a softmax warp can be one
+    // key tile ahead of the slowest one (tile j+2 needs S(j+2), which waits
+    // for P(j) V(j)), so consecutive tiles must not share a barrier phase
+    const uint32_t bar_s0 = base + kTcBar, bar_s1 = bar_s0 + 8, bar_o = bar_s0 + 16, bar_p0 = bar_s0 + 24,
+                   bar_last = bar_s0 + 40, bar_fin = bar_s0 + 48;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + (base - raw) + kTcBar + 56);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const AttnTile t = tiles[blockIdx.x];
     const int head = blockIdx.y;
     const int tid = threadIdx.x, warp = tid >> 5;
+    const uint32_t lane = tid & 31;
     const __half* qh = q + static_cast<int64_t>(t.q_row0) * ldq + head * kDH;
     const __half* kh = k + static_cast<int64_t>(t.k_row0) * ldk + head * kDH;
     const __half* vh = v + static_cast<int64_t>(t.k_row0) * ldv + head * kDH;
@@ -493,6 +539,9 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
         mbar_init(bar_s0, 1);
         mbar_init(bar_s1, 1);
         mbar_init(bar_o, 1);
+        mbar_init(bar_p0, 4);
+        mbar_init(bar_p0 + 8, 4);
+        mbar_init(bar_last, 1);
         mbar_init(bar_fin, 1);
         *abort_flag = 0u;
         fence_barrier_init();
@@ -501,176 +550,208 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
         tmem_alloc(tmem_slot, kTcTmemCols);
         tc_fence_before();
     }
-    // zero padding: dims 72..79 (chunk 1 of K-atom 1) of Q and both K buffers,
-    // V^T rows 72..79
-    for (int r = tid; r < 128; r += kTcThreads) sts_v4(sQ + 128u * 128u + sw128(r, 1), 0, 0, 0, 0);
-    for (int i = tid; i < 128; i += kTcThreads) {
-        const uint32_t r = i & 63, b = i >> 6;
-        sts_v4(sK + b * kTcKBuf + 64u * 128u + sw128(r, 1), 0, 0, 0, 0);
+    if (warp < 4) {
+        // constant parts: dims 72..79 (chunk 1 of K-atom 1) of Q and both K
+        // buffers are zero; in both V^T buffers row 72 is ones (the row-sum
+        // column) and rows 73..79 zero
+        sts_v4(sQ + 128u * 128u + sw128(tid, 1), 0, 0, 0, 0);
+        {
+            const uint32_t r = tid & 63, b = tid >> 6;
+            sts_v4(sK + b * kTcKBuf + 64u * 128u + sw128(r, 1), 0, 0, 0, 0);
+            const uint32_t i = tid & 63;
+            const uint32_t one2 = i < 8 ? 0x3C003C00u : 0u;   // fp16 1.0 pairs
+            sts_v4(sV + b * kTcVBuf + (72u + (i >> 3)) * 128u + 16u * (i & 7), one2, one2, one2, one2);
+        }
+        // Q: thread tid copies row tid
+        const bool ok = tid < t.q_rows;
+        const __half* g = qh + (ok ? static_cast<int64_t>(tid) * ldq : 0);
+#pragma unroll
+        for (uint32_t c = 0; c < 9; ++c) cp_async16_at(tc_chunk_addr(sQ, 128, tid, c), g + 8 * c, ok);
+    } else {
+        tc_load_k(sK, kh, ldk, min(kKT, t.k_len), lane);
+        if (n_kt > 1) tc_load_k(sK + kTcKBuf, kh + static_cast<int64_t>(kKT) * ldk, ldk, min(kKT, t.k_len - kKT), lane);
+        VStage v0;
+        tc_fetch_v(v0, vh, ldv, min(kKT, t.k_len), lane);
+        tc_store_vt(v0, sV, lane);
+        if (n_kt > 1) {
+            tc_fetch_v(v0, vh + static_cast<int64_t>(kKT) * ldv, ldv, min(kKT, t.k_len - kKT), lane);
+            tc_store_vt(v0, sV + kTcVBuf, lane);
+        }
     }
-    for (int i = tid; i < 64; i += kTcThreads) sts_v4(sV + (72u + (i >> 3)) * 128u + 16u * (i & 7), 0, 0, 0, 0);
-
-    tc_load_rows(sQ, 128, qh, ldq, t.q_rows);
-    tc_load_rows(sK, 64, kh, ldk, min(kKT, t.k_len));
     cp_async_commit();
-    VStage vs;
-    tc_fetch_v(vs, vh, ldv, min(kKT, t.k_len));
     cp_async_wait<0>();
     fence_proxy_async_smem();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    if (tid == 0 && !stall) {
-        tc_issue_scores(tmem, sQ, sK);
-        mma_commit(bar_s0);
-    }
-    if (n_kt > 1) {
-        tc_load_rows(sK + kTcKBuf, 64, kh + static_cast<int64_t>(kKT) * ldk, ldk, min(kKT, t.k_len - kKT));
-        cp_async_commit();
-    }
 
-    float o[kDH];
+    if (warp < 4) {
+        // ---------------------------------------------------------- softmax
+        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        float m_ref = -INFINITY;
+        bool done = false;
+        for (int j = 0; j < n_kt; ++j) {
+            const uint32_t b = j & 1;
+            const uint32_t tbuf = tmem + lane_base + 64u * b;
+            if (!tc_warp_wait(b ? bar_s1 : bar_s0, (j >> 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull))
+                break;
+            tc_fence_after();
+            float s[64];
+            {
+                uint32_t r0[32], r1[32];
+                tmem_ld_32x32b_x32(tbuf, r0);
+                tmem_ld_32x32b_x32(tbuf + 32u, r1);
+                tmem_ld_wait();
 #pragma unroll
-    for (int d = 0; d < kDH; ++d) o[d] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f;
-    bool failed = false, finished = false;
-
-    for (int kt = 0; kt < n_kt; ++kt) {
-        const uint32_t b = kt & 1;
-        // [A]
-        cp_async_wait<0>();
-        fence_proxy_async_smem();
-        tc_fence_before();
-        if (__syncthreads_or(failed)) break;
-        tc_fence_after();
-        if (tid == 0 && !stall && kt + 1 < n_kt) {
-            tc_issue_scores(tmem + 64u * (b ^ 1u), sQ, sK + kTcKBuf * (b ^ 1u));
-            mma_commit(b ? bar_s0 : bar_s1);
-        }
-        // [B]
-        if (!mbar_wait(b ? bar_s1 : bar_s0, (kt >> 1) & 1, abort_flag, timeout_ns)) {
-            tc_raise(err, abort_flag, kDevTimeoutTmemFull);
-            failed = true;
-        }
-        tc_fence_after();
-        float s[64];
-        {
-            uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + 64u * b, r0);
-            tmem_ld_32x32b_x32(tmem + lane_base + 64u * b + 32u, r1);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                s[i] = __uint_as_float(r0[i]);
-                s[32 + i] = __uint_as_float(r1[i]);
+                for (int i = 0; i < 32; ++i) {
+                    s[i] = __uint_as_float(r0[i]);
+                    s[32 + i] = __uint_as_float(r1[i]);
+                }
             }
-        }
-        if (kt + 2 < n_kt) {
-            const int k0 = (kt + 2) * kKT;
-            tc_load_rows(sK + kTcKBuf * b, 64, kh + static_cast<int64_t>(k0) * ldk, ldk, min(kKT, t.k_len - k0));
-            cp_async_commit();
-        }
-        const int valid = t.k_len - kt * kKT;   // keys of this tile that exist (>= 1)
-        float mx = m_run;
+            const int valid = t.k_len - j * kKT;   // keys of this tile that exist (>= 1)
+            if (valid < kKT) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-            float x = s[i] * scale_log2;
-            if (i >= valid) x = -INFINITY;
-            s[i] = x;
-            mx = fmaxf(mx, x);
-        }
-        const float corr = exp2f(m_run - mx);
-        float rowsum = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-            s[i] = exp2f(s[i] - mx);
-            rowsum += s[i];
-        }
-        l_run = l_run * corr + rowsum;
-        m_run = mx;
-        // [C]
-        if (kt > 0) {
-            if (!mbar_wait(bar_o, (kt - 1) & 1, abort_flag, timeout_ns)) {
-                tc_raise(err, abort_flag, kDevTimeoutTmemFull);
-                failed = true;
+                for (int i = 0; i < 64; ++i)
+                    if (i >= valid) s[i] = -INFINITY;
             }
+            float mx;
+            {   // row maximum of the raw scores (a tree, not a 64-deep chain)
+                float m8[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    m8[i] = fmaxf(fmaxf(fmaxf(s[i], s[i + 8]), fmaxf(s[i + 16], s[i + 24])),
+                                  fmaxf(fmaxf(s[i + 32], s[i + 40]), fmaxf(s[i + 48], s[i + 56])));
+                mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                           fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            }
+            const float m_new = mx * scale_log2;
+            const bool move = m_new > m_ref + 8.0f;
+            float corr = 1.0f;
+            if (move) {
+                corr = ex2_approx(m_ref - m_new);   // 0 on the first tile
+                m_ref = m_new;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, move)) {
+                // O holds P(0..j-1) V against the old reference: wait for the
+                // last of those products (S(j) was issued after P(j-2) V(j-2)
+                // completed, so this parity names P(j-1) V(j-1))
+                if (!tc_warp_wait(bar_o, (j - 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull)) break;
+                tc_fence_after();
+                tc_scale_o(tmem + lane_base + kTcColO, corr);
+            }
+            {   // P over S(j): column c of P_hi / P_lo holds keys 2c, 2c+1
+                uint32_t hi[32], lo[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const float p0 = ex2_approx(__fmaf_rn(s[2 * c], scale_log2, -m_ref));
+                    const float p1 = ex2_approx(__fmaf_rn(s[2 * c + 1], scale_log2, -m_ref));
+                    split_half2(p0, p1, hi[c], lo[c]);
+                }
+                tmem_st_32x32b_x32(tbuf, hi);
+                tmem_st_32x32b_x32(tbuf + 32u, lo);
+                tmem_st_wait();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_p0 + 8u * b);
+            done = j + 1 == n_kt;
+        }
+        if (done && tc_warp_wait(bar_last, 0, abort_flag, timeout_ns, err, kDevTimeoutTmemFull)) {
             tc_fence_after();
             uint32_t r0[32], r1[32], r2[16];
             tmem_ld_32x32b_x32(tmem + lane_base + kTcColO, r0);
             tmem_ld_32x32b_x32(tmem + lane_base + kTcColO + 32u, r1);
             tmem_ld_32x32b_x16(tmem + lane_base + kTcColO + 64u, r2);
             tmem_ld_wait();
+            if (tid < t.q_rows) {
+                const float l = __uint_as_float(r2[8]);
+                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                float* dst = out + static_cast<int64_t>(t.o_row0 + tid) * ldo + head * kDH;
 #pragma unroll
-            for (int d = 0; d < 32; ++d) {
-                o[d] = (o[d] + __uint_as_float(r0[d])) * corr;
-                o[32 + d] = (o[32 + d] + __uint_as_float(r1[d])) * corr;
+                for (int d = 0; d < 32; d += 2) {
+                    *reinterpret_cast<float2*>(dst + d) =
+                        make_float2(__uint_as_float(r0[d]) * inv, __uint_as_float(r0[d + 1]) * inv);
+                    *reinterpret_cast<float2*>(dst + 32 + d) =
+                        make_float2(__uint_as_float(r1[d]) * inv, __uint_as_float(r1[d + 1]) * inv);
+                }
+#pragma unroll
+                for (int d = 0; d < 8; d += 2)
+                    *reinterpret_cast<float2*>(dst + 64 + d) =
+                        make_float2(__uint_as_float(r2[d]) * inv, __uint_as_float(r2[d + 1]) * inv);
             }
-#pragma unroll
-            for (int d = 0; d < 8; ++d) o[64 + d] = (o[64 + d] + __uint_as_float(r2[d])) * corr;
         }
-        // [D]
-        tc_store_vt(vs, sV);
-        if (kt + 1 < n_kt) {
-            const int k0 = (kt + 1) * kKT;
-            tc_fetch_v(vs, vh + static_cast<int64_t>(k0) * ldv, ldv, min(kKT, t.k_len - k0));
+    } else {
+        // ---------------------------------------------------------- control
+        const bool issuer = lane == 0 && !stall;
+        if (issuer) {
+            tc_issue_scores(tmem, sQ, sK);
+            mma_commit(bar_s0);
+            if (n_kt > 1) {
+                tc_issue_scores(tmem + 64u, sQ, sK + kTcKBuf);
+                mma_commit(bar_s1);
+            }
         }
-        // [E] row tid of P: keys 8c .. 8c+7 in chunk c
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            uint32_t hi[4], lo[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) split_half2(s[8 * c + 2 * e], s[8 * c + 2 * e + 1], hi[e], lo[e]);
-            sts_v4(sPH + sw128(tid, c), hi[0], hi[1], hi[2], hi[3]);
-            sts_v4(sPL + sw128(tid, c), lo[0], lo[1], lo[2], lo[3]);
+        __syncwarp();
+        VStage vs;
+        if (n_kt > 2) tc_fetch_v(vs, vh + static_cast<int64_t>(2 * kKT) * ldv, ldv, min(kKT, t.k_len - 2 * kKT), lane);
+        bool ok = true;
+        if (n_kt > 2) {   // K tile 2 into K buffer 0 once S(0) has read it
+            ok = tc_warp_wait(bar_s0, 0, abort_flag, timeout_ns, err, kDevTimeoutTmemFull);
+            if (ok) {
+                tc_load_k(sK, kh + static_cast<int64_t>(2 * kKT) * ldk, ldk, min(kKT, t.k_len - 2 * kKT), lane);
+                cp_async_commit();
+            }
         }
-        // [F]
-        fence_proxy_async_smem();
-        tc_fence_before();
-        if (__syncthreads_or(failed)) break;
-        tc_fence_after();
-        if (tid == 0 && !stall) {
-            tc_issue_pv(tmem + kTcColO, sPH, sPL, sV);
-            mma_commit(bar_o);
-        }
-        finished = kt + 1 == n_kt;
-    }
-
-    if (finished) {
-        if (!mbar_wait(bar_o, (n_kt - 1) & 1, abort_flag, timeout_ns)) {
-            tc_raise(err, abort_flag, kDevTimeoutTmemFull);
-            failed = true;
-        }
-        tc_fence_after();
-        uint32_t r0[32], r1[32], r2[16];
-        tmem_ld_32x32b_x32(tmem + lane_base + kTcColO, r0);
-        tmem_ld_32x32b_x32(tmem + lane_base + kTcColO + 32u, r1);
-        tmem_ld_32x32b_x16(tmem + lane_base + kTcColO + 64u, r2);
-        tmem_ld_wait();
-#pragma unroll
-        for (int d = 0; d < 32; ++d) {
-            o[d] += __uint_as_float(r0[d]);
-            o[32 + d] += __uint_as_float(r1[d]);
-        }
-#pragma unroll
-        for (int d = 0; d < 8; ++d) o[64 + d] += __uint_as_float(r2[d]);
-        if (!failed && tid < t.q_rows) {
-            const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-            float* dst = out + static_cast<int64_t>(t.o_row0 + tid) * ldo + head * kDH;
-#pragma unroll
-            for (int d = 0; d < kDH; d += 2)
-                *reinterpret_cast<float2*>(dst + d) = make_float2(o[d] * inv, o[d + 1] * inv);
+        for (int j = 0; ok && j < n_kt; ++j) {
+            const uint32_t b = j & 1;
+            if (!tc_warp_wait(bar_p0 + 8u * b, (j >> 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutEmpty)) break;
+            tc_fence_after();
+            if (issuer) {
+                tc_issue_pv(tmem + kTcColO, tmem + 64u * b, sV + kTcVBuf * b, j > 0);
+                mma_commit(bar_o);
+                if (j + 1 == n_kt) mma_commit(bar_last);
+            }
+            __syncwarp();
+            if (j + 2 < n_kt) {
+                // P(j) V(j) done: TMEM buffer b and V^T buffer b are free
+                if (!tc_warp_wait(bar_o, j & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull)) break;
+                tc_fence_after();
+                cp_async_wait<0>();   // K tile j+2 (loaded during the previous iteration)
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (issuer) {
+                    tc_issue_scores(tmem + 64u * b, sQ, sK + kTcKBuf * b);
+                    mma_commit(b ? bar_s1 : bar_s0);
+                }
+                tc_store_vt(vs, sV + kTcVBuf * b, lane);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (j + 3 < n_kt) {
+                    const int k0 = (j + 3) * kKT;
+                    tc_fetch_v(vs, vh + static_cast<int64_t>(k0) * ldv, ldv, min(kKT, t.k_len - k0), lane);
+                }
+            }
+            if (j + 3 < n_kt) {   // K tile j+3 into K buffer (j+1) % 2 once S(j+1) has read it
+                const uint32_t b1 = b ^ 1u;
+                if (!tc_warp_wait(b1 ? bar_s1 : bar_s0, ((j + 1) >> 1) & 1, abort_flag, timeout_ns, err,
+                                  kDevTimeoutTmemFull))
+                    break;
+                const int k0 = (j + 3) * kKT;
+                tc_load_k(sK + kTcKBuf * b1, kh + static_cast<int64_t>(k0) * ldk, ldk, min(kKT, t.k_len - k0), lane);
+                cp_async_commit();
+            }
         }
     }
 
     // Release: no copy in flight into shared memory, every MMA this CTA
-    // issued retired (the commit below arrives once they all have), every
-    // TMEM load landed.
+    // issued retired (the issuer's commit below arrives once they all have),
+    // every TMEM access landed.
     cp_async_wait<0>();
     tmem_ld_wait();
+    tmem_st_wait();
     tc_fence_before();
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 128) {
         tc_fence_after();
         mma_commit(bar_fin);
         volatile uint32_t no_abort = 0;
