@@ -341,22 +341,25 @@ attention_exact_kernel(const __half* __restrict__ q, int64_t ldq, const __half* 
 
 // ---------------------------------------------------------------------------
 // tcgen05 kernel.  Shared memory (from a 1024-byte aligned base), every
-// operand K-major with the 128-byte swizzle (row r at r * 128 bytes, its
-// 16-byte chunk c stored at chunk c ^ (r % 8)), written by the threads
-// themselves:
-//   Q       [2 K-atoms][128 rows][128 B]  dims 0..63 | 64..79 (72..79 zero)
-//   K[2]    [2 K-atoms][ 64 rows][128 B]  key tiles j % 2
-//   V^T[2]  [80 rows (dims)][128 B = 64 keys]   row 72 ones, 73..79 zero
+// operand with the 128-byte swizzle (a 128-byte row's 16-byte chunk c stored
+// at chunk c ^ (row % 8)), filled by cp.async, three key tiles in flight:
+//   K[3]  K-major [2 atoms][64 rows][128 B]: dims 0..63 | 64..79 (72..79 zero)
+//   V[3]  MN-major [2 atoms][64 keys][128 B]: dims 0..63 | 64..127 of each
+//         key row as loaded (no transpose); in atom 1 only dims 64..79 are
+//         read: 64..71 loaded, 72 = 1.0 (the row-sum column), 73..79 zero
 // TMEM (256 columns): two 64-column buffers, each holding first the scores
 // S(j) of key tile j (fp32) and then, over them, its probabilities as the A
 // operand of P V: P_hi in columns 0..31 and P_lo in 32..63 (fp16 pairs);
 // the output accumulator O (80 columns; column 72 = running row sum) at
-// column 128.
-constexpr int kTcThreads = 160;   // warps 0-3: softmax (one query row each), warp 4: loads + MMA issue
-constexpr uint32_t kTcQ = 0, kTcK = 32768, kTcKBuf = 16384, kTcV = 65536, kTcVBuf = 10240;
-constexpr uint32_t kTcBar = 86016;
-constexpr int kTcSmem = static_cast<int>(kTcBar) + 64 + 1024;   // 7 barriers, TMEM slot, abort flag
-constexpr uint32_t kTcTmemCols = 256, kTcColO = 128;
+// column 128; Q (the A operand of the scores: 80 dims as fp16 pairs, dims
+// 72..79 zero) at column 208.
+constexpr int kTcThreads = 192;   // warps 0-3: softmax (one query row each), 4: MMA issue, 5: loads
+constexpr int kTcStages = 3;
+constexpr uint32_t kTcK = 0, kTcKBuf = 16384, kTcV = 49152, kTcVBuf = 16384;
+constexpr uint32_t kTcBar = 98304;
+constexpr int kTcSmem = static_cast<int>(kTcBar) + 192 + 1024;   // 20 barriers, TMEM slot, abort flag
+constexpr uint32_t kTcTmemCols = 256, kTcColO = 128, kTcColQ = 208;
+constexpr uint32_t kTcOutPitch = 304;   // bytes per staged output row (76 floats)
 
 __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
     return row * 128u + (((chunk ^ row) & 7u) << 4);
@@ -364,15 +367,13 @@ __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
 __device__ __forceinline__ void sts_v4(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
 }
-__device__ __forceinline__ void sts_b32(uint32_t a, uint32_t x) {
-    asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(x) : "memory");
-}
 __device__ __forceinline__ void cp_async16_at(uint32_t dst, const void* gmem, bool valid) {
     const int bytes = valid ? 16 : 0;
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(gmem), "r"(bytes) : "memory");
 }
-// Writes of the generic proxy (st.shared, completed cp.async) become visible
-// to the tensor core's reads after this fence and a barrier.
+// Writes of the generic proxy (st.shared, cp.async) are ordered before the
+// tensor core's reads by this fence (with a barrier between writer and
+// issuer).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -382,82 +383,51 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// Row r of a 72-wide fp16 operand into a K-major region of `rows` rows:
-// chunks 0..7 (dims 0..63) in K-atom 0, chunk 8 (dims 64..71) as chunk 0 of
-// K-atom 1.
-__device__ __forceinline__ uint32_t tc_chunk_addr(uint32_t region, uint32_t rows, uint32_t r, uint32_t c) {
-    return c < 8 ? region + sw128(r, c) : region + rows * 128u + sw128(r, 0);
+// Row r of a 72-wide fp16 operand in a two-atom region of 64 rows: chunks
+// 0..7 (dims 0..63) in atom 0, chunk 8 (dims 64..71) as chunk 0 of atom 1.
+// The same addresses serve the K-major (K) and MN-major (V) operands: only
+// the descriptors differ.
+__device__ __forceinline__ uint32_t tc_chunk_addr(uint32_t region, uint32_t r, uint32_t c) {
+    return c < 8 ? region + sw128(r, c) : region + 64u * 128u + sw128(r, 0);
 }
 
-// Key tile into a K buffer by the control warp: lane l copies rows l and
-// l + 32; rows >= valid are zeros.
-__device__ __forceinline__ void tc_load_k(uint32_t buf, const __half* src, int64_t ld, int valid, uint32_t lane) {
+// A 64-row key tile (K or V) by the loader warp: lane l copies rows l and
+// l + 32; rows >= valid are zeros (their scores are masked, their
+// probabilities 0, and 0 x garbage could be NaN).
+__device__ __forceinline__ void tc_load_tile(uint32_t buf, const __half* src, int64_t ld, int valid, uint32_t lane) {
 #pragma unroll
     for (uint32_t h = 0; h < 2; ++h) {
         const uint32_t r = lane + 32u * h;
         const bool ok = static_cast<int>(r) < valid;
         const __half* g = src + (ok ? static_cast<int64_t>(r) * ld : 0);
 #pragma unroll
-        for (uint32_t c = 0; c < 9; ++c) cp_async16_at(tc_chunk_addr(buf, 64, r, c), g + 8 * c, ok);
+        for (uint32_t c = 0; c < 9; ++c) cp_async16_at(tc_chunk_addr(buf, r, c), g + 8 * c, ok);
     }
 }
 
-// A key tile of V in the control warp's registers on its way to V^T: lane j
-// holds keys 2j and 2j+1 (all 72 dims).  Keys >= valid are zeros (their
-// probabilities are 0, and 0 x garbage could be NaN).
-struct VStage {
-    uint4 a[9], b[9];
-};
-__device__ __forceinline__ void tc_fetch_v(VStage& st, const __half* src, int64_t ld, int valid, uint32_t j) {
-    const bool ok0 = static_cast<int>(2 * j) < valid, ok1 = static_cast<int>(2 * j + 1) < valid;
-    const __half* r0 = src + (ok0 ? static_cast<int64_t>(2 * j) * ld : 0);
-    const __half* r1 = src + (ok1 ? static_cast<int64_t>(2 * j + 1) * ld : 0);
-#pragma unroll
-    for (int c = 0; c < 9; ++c) {
-        st.a[c] = ok0 ? __ldg(reinterpret_cast<const uint4*>(r0 + 8 * c)) : make_uint4(0, 0, 0, 0);
-        st.b[c] = ok1 ? __ldg(reinterpret_cast<const uint4*>(r1 + 8 * c)) : make_uint4(0, 0, 0, 0);
-    }
-}
-// V^T row d = 8c + e holds keys 2j, 2j+1 in the 32-bit word at byte 4j:
-// chunk j / 4 (swizzled by d % 8 = e), word j % 4.  Each store instruction
-// writes one row's 32 words: all 32 banks, no conflicts.
-__device__ __forceinline__ void tc_store_vt(const VStage& st, uint32_t vt, uint32_t j) {
-#pragma unroll
-    for (uint32_t c = 0; c < 9; ++c) {
-        const uint32_t aw[4] = {st.a[c].x, st.a[c].y, st.a[c].z, st.a[c].w};
-        const uint32_t bw[4] = {st.b[c].x, st.b[c].y, st.b[c].z, st.b[c].w};
-        const uint32_t row0 = vt + 8u * c * 128u + 4u * (j & 3u);
-#pragma unroll
-        for (uint32_t e = 0; e < 8; ++e) {
-            const uint32_t word = __byte_perm(aw[e >> 1], bw[e >> 1], (e & 1) ? 0x7632u : 0x5410u);
-            sts_b32(row0 + e * 128u + ((((j >> 2) ^ e) & 7u) << 4), word);
-        }
-    }
-}
-
-// S(128 x 64) = Q K^T over the 80 padded dims: four K = 16 steps inside
-// K-atom 0 (start address + 32 bytes each) and one in K-atom 1.
-__device__ __forceinline__ void tc_issue_scores(uint32_t tmem_s, uint32_t q, uint32_t k) {
+// S(128 x 64) = Q K^T over the 80 padded dims: Q from TMEM (16 dims = 8
+// columns per step), K K-major: four steps inside atom 0 (start address + 32
+// bytes each) and one in atom 1.
+__device__ __forceinline__ void tc_issue_scores(uint32_t tmem_s, uint32_t tmem_q, uint32_t k) {
     constexpr uint32_t idesc = idesc_f16_f32(128, 64);
 #pragma unroll
     for (uint32_t ks = 0; ks < 5; ++ks) {
-        const uint32_t qa = ks < 4 ? q + 32u * ks : q + 128u * 128u;
         const uint32_t kb = ks < 4 ? k + 32u * ks : k + 64u * 128u;
-        mma_f16(tmem_s, smem_desc_k_sw128(qa), smem_desc_k_sw128(kb), idesc, ks > 0 ? 1u : 0u);
+        mma_f16_ts(tmem_s, tmem_q + 8u * ks, smem_desc_k_sw128(kb), idesc, ks > 0 ? 1u : 0u);
     }
 }
-// O(128 x 80) (+)= P_hi V + P_lo V over the tile's 64 keys, P from TMEM
-// (16 keys = 8 columns per step).  Row 72 of V^T is all ones, so column 72
-// of O accumulates the row sums of P.
-__device__ __forceinline__ void tc_issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint32_t vt, bool accumulate) {
-    constexpr uint32_t idesc = idesc_f16_f32(128, 80);
+// O(128 x 80) (+)= P_hi V + P_lo V over the tile's 64 keys: P from TMEM
+// (16 keys = 8 columns per step), V MN-major (16 keys = two 1024-byte
+// atoms per step, dims 64..79 in the atom 8 KB on).
+__device__ __forceinline__ void tc_issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint32_t v, bool accumulate) {
+    constexpr uint32_t idesc = idesc_f16_f32(128, 80) | kIdescBMajorMN;
 #pragma unroll
     for (uint32_t ks = 0; ks < 4; ++ks)
-        mma_f16_ts(tmem_o, tmem_p + 8u * ks, smem_desc_k_sw128(vt + 32u * ks), idesc,
+        mma_f16_ts(tmem_o, tmem_p + 8u * ks, smem_desc_mn_sw128(v + 2048u * ks, 8192u), idesc,
                    (accumulate || ks > 0) ? 1u : 0u);
 #pragma unroll
     for (uint32_t ks = 0; ks < 4; ++ks)
-        mma_f16_ts(tmem_o, tmem_p + 32u + 8u * ks, smem_desc_k_sw128(vt + 32u * ks), idesc, 1u);
+        mma_f16_ts(tmem_o, tmem_p + 32u + 8u * ks, smem_desc_mn_sw128(v + 2048u * ks, 8192u), idesc, 1u);
 }
 
 // Bounded wait taken by a whole warp: the warp goes on only if every lane's
@@ -492,21 +462,29 @@ __device__ __forceinline__ void tc_scale_o(uint32_t taddr, float f) {
 }
 
 // Roles and hand-offs (mbarriers; no block-wide barrier inside the key loop).
-// Key tile j uses TMEM buffer, K buffer and V^T buffer j % 2.
-//   control warp, per key tile j:
-//     wait until the four softmax warps have written P(j); issue
-//     O (+)= P(j) V(j); once that is done (P(j) and V^T(j) read), issue
-//     S(j+2) into the same TMEM buffer (its K tile was loaded one iteration
-//     earlier) and store V tile j+2 (fetched one tile ahead into registers)
-//     to V^T; once S(j+1) has read its K buffer, load K tile j+3 into it.
+// Key tile j uses TMEM buffer j % 2 and K / V buffers j % 3; every barrier
+// named "[b]" exists once per buffer, so no waiter can be overtaken by the
+// next phase of the barrier it waits on.
+//   loader warp, per key tile j: once S(j-3) has read K buffer j % 3
+//     (k_empty), issue the cp.async of K tile j (k_full completes when they
+//     land); once P(j-3) V(j-3) has read V buffer j % 3 (v_empty), the same
+//     for V tile j (v_full).  It never waits for its own copies.
+//   MMA warp, per key tile j: wait for P(j) (p_full, four softmax warps)
+//     and V tile j; issue O (+)= P(j) V(j) (commits o_full, v_empty); once
+//     K tile j+2 has landed, issue S(j+2) into the same TMEM buffer right
+//     behind it (commits s_full, k_empty): the tensor core executes one
+//     thread's MMAs in issue order, so S(j+2) writes only after P(j) V(j)
+//     has read P(j), and the MMA warp never waits for a product.
 //   softmax warps (thread = query row = TMEM lane), per key tile j:
 //     wait for S(j), read the row, mask, row max, probabilities
 //     p = exp2(s * scale_log2 - m) against a reference m that moves only
 //     when the row's maximum exceeds it by more than 8 (so p <= 256, exact
 //     in the fp16 split); if m moved, wait for P(j-1) V(j-1) and rescale the
-//     row of O in TMEM; write P_hi / P_lo over S(j); signal.
+//     row of O in TMEM; write P_hi / P_lo over S(j); signal p_full.
 // The softmax warps never wait for a P V product in the steady state, so
-// the score tiles stream through them while the tensor core runs behind.
+// the score tiles stream through them while the tensor core runs behind; a
+// softmax warp can be one key tile ahead of the slowest one (tile j+2 needs
+// S(j+2), which waits for P(j) V(j)).
 // Every wait is bounded; an expired wait records its code, raises the CTA's
 // abort flag (every other wait then gives up too), and the roles unwind.
 __global__ void __launch_bounds__(kTcThreads, 2)
@@ -517,13 +495,12 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     extern __shared__ __align__(1024) uint8_t tc_smem[];
     const uint32_t raw = smem_u32(tc_smem);
     const uint32_t base = (raw + 1023u) & ~1023u;
-    const uint32_t sQ = base + kTcQ, sK = base + kTcK, sV = base + kTcV;
-    // P(j) is signalled on bar_p0 + 8 * (j % 2): a softmax warp can be one
-    // key tile ahead of the slowest one (tile j+2 needs S(j+2), which waits
-    // for P(j) V(j)), so consecutive tiles must not share a barrier phase
-    const uint32_t bar_s0 = base + kTcBar, bar_s1 = bar_s0 + 8, bar_o = bar_s0 + 16, bar_p0 = bar_s0 + 24,
-                   bar_last = bar_s0 + 40, bar_fin = bar_s0 + 48;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + (base - raw) + kTcBar + 56);
+    const uint32_t sK = base + kTcK, sV = base + kTcV;
+    // per-buffer barriers: bar + 8 * buffer
+    const uint32_t bar_s = base + kTcBar, bar_p = bar_s + 16, bar_kf = bar_s + 32, bar_vf = bar_s + 56,
+                   bar_ke = bar_s + 80, bar_ve = bar_s + 104, bar_o = bar_s + 128, bar_last = bar_s + 136,
+                   bar_q = bar_s + 144, bar_fin = bar_s + 152;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + (base - raw) + kTcBar + 160);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const AttnTile t = tiles[blockIdx.x];
@@ -536,12 +513,19 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     const int n_kt = (t.k_len + kKT - 1) / kKT;
 
     if (tid == 0) {
-        mbar_init(bar_s0, 1);
-        mbar_init(bar_s1, 1);
+        for (uint32_t b = 0; b < 2; ++b) {
+            mbar_init(bar_s + 8 * b, 1);
+            mbar_init(bar_p + 8 * b, 4);
+        }
+        for (uint32_t b = 0; b < kTcStages; ++b) {
+            mbar_init(bar_kf + 8 * b, 32);   // one cp.async arrival per loader lane
+            mbar_init(bar_vf + 8 * b, 32);
+            mbar_init(bar_ke + 8 * b, 1);
+            mbar_init(bar_ve + 8 * b, 1);
+        }
         mbar_init(bar_o, 1);
-        mbar_init(bar_p0, 4);
-        mbar_init(bar_p0 + 8, 4);
         mbar_init(bar_last, 1);
+        mbar_init(bar_q, 4);
         mbar_init(bar_fin, 1);
         *abort_flag = 0u;
         fence_barrier_init();
@@ -550,37 +534,29 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
         tmem_alloc(tmem_slot, kTcTmemCols);
         tc_fence_before();
     }
+    uint4 qv[9];
     if (warp < 4) {
-        // constant parts: dims 72..79 (chunk 1 of K-atom 1) of Q and both K
-        // buffers are zero; in both V^T buffers row 72 is ones (the row-sum
-        // column) and rows 73..79 zero
-        sts_v4(sQ + 128u * 128u + sw128(tid, 1), 0, 0, 0, 0);
-        {
-            const uint32_t r = tid & 63, b = tid >> 6;
+        // constant parts: dims 72..79 (chunk 1 of atom 1) are zero in every
+        // K buffer and hold 1.0 at dim 72 in every V buffer
+        for (uint32_t i = tid; i < kTcStages * 64u; i += 128u) {
+            const uint32_t r = i & 63u, b = i >> 6;
             sts_v4(sK + b * kTcKBuf + 64u * 128u + sw128(r, 1), 0, 0, 0, 0);
-            const uint32_t i = tid & 63;
-            const uint32_t one2 = i < 8 ? 0x3C003C00u : 0u;   // fp16 1.0 pairs
-            sts_v4(sV + b * kTcVBuf + (72u + (i >> 3)) * 128u + 16u * (i & 7), one2, one2, one2, one2);
+            sts_v4(sV + b * kTcVBuf + 64u * 128u + sw128(r, 1), 0x00003C00u, 0, 0, 0);
         }
-        // Q: thread tid copies row tid
+        fence_proxy_async_smem();
+        // this thread's query row (zeros past the tile), into TMEM below
         const bool ok = tid < t.q_rows;
-        const __half* g = qh + (ok ? static_cast<int64_t>(tid) * ldq : 0);
+        const uint4* g = reinterpret_cast<const uint4*>(qh + (ok ? static_cast<int64_t>(tid) * ldq : 0));
 #pragma unroll
-        for (uint32_t c = 0; c < 9; ++c) cp_async16_at(tc_chunk_addr(sQ, 128, tid, c), g + 8 * c, ok);
-    } else {
-        tc_load_k(sK, kh, ldk, min(kKT, t.k_len), lane);
-        if (n_kt > 1) tc_load_k(sK + kTcKBuf, kh + static_cast<int64_t>(kKT) * ldk, ldk, min(kKT, t.k_len - kKT), lane);
-        VStage v0;
-        tc_fetch_v(v0, vh, ldv, min(kKT, t.k_len), lane);
-        tc_store_vt(v0, sV, lane);
-        if (n_kt > 1) {
-            tc_fetch_v(v0, vh + static_cast<int64_t>(kKT) * ldv, ldv, min(kKT, t.k_len - kKT), lane);
-            tc_store_vt(v0, sV + kTcVBuf, lane);
+        for (int c = 0; c < 9; ++c) qv[c] = ok ? __ldg(g + c) : make_uint4(0, 0, 0, 0);
+    } else if (warp == 5) {
+        // key tiles 0 .. 2 (their arrivals follow the barrier below)
+        for (int j = 0; j < kTcStages && j < n_kt; ++j) {
+            const int k0 = j * kKT, valid = min(kKT, t.k_len - k0);
+            tc_load_tile(sK + kTcKBuf * j, kh + static_cast<int64_t>(k0) * ldk, ldk, valid, lane);
+            tc_load_tile(sV + kTcVBuf * j, vh + static_cast<int64_t>(k0) * ldv, ldv, valid, lane);
         }
     }
-    cp_async_commit();
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
@@ -588,13 +564,34 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     if (warp < 4) {
         // ---------------------------------------------------------- softmax
         const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        {   // Q row into TMEM: column c holds dims 2c, 2c+1
+            uint32_t r0[32], r1[16];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                r0[4 * c] = qv[c].x;
+                r0[4 * c + 1] = qv[c].y;
+                r0[4 * c + 2] = qv[c].z;
+                r0[4 * c + 3] = qv[c].w;
+            }
+            r1[0] = qv[8].x;
+            r1[1] = qv[8].y;
+            r1[2] = qv[8].z;
+            r1[3] = qv[8].w;
+#pragma unroll
+            for (int c = 4; c < 16; ++c) r1[c] = 0u;
+            tmem_st_32x32b_x32(tmem + lane_base + kTcColQ, r0);
+            tmem_st_32x32b_x16(tmem + lane_base + kTcColQ + 32u, r1);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_q);
+        }
         float m_ref = -INFINITY;
         bool done = false;
         for (int j = 0; j < n_kt; ++j) {
             const uint32_t b = j & 1;
             const uint32_t tbuf = tmem + lane_base + 64u * b;
-            if (!tc_warp_wait(b ? bar_s1 : bar_s0, (j >> 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull))
-                break;
+            if (!tc_warp_wait(bar_s + 8u * b, (j >> 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull)) break;
             tc_fence_after();
             float s[64];
             {
@@ -633,8 +630,10 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
             }
             if (j > 0 && __any_sync(0xffffffffu, move)) {
                 // O holds P(0..j-1) V against the old reference: wait for the
-                // last of those products (S(j) was issued after P(j-2) V(j-2)
-                // completed, so this parity names P(j-1) V(j-1))
+                // last of those products.  S(j) was committed after P(j-2) V
+                // was issued, and a commit arrives only once every earlier
+                // MMA of its thread is done, so P(0..j-2) V are complete and
+                // this parity names P(j-1) V(j-1)
                 if (!tc_warp_wait(bar_o, (j - 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull)) break;
                 tc_fence_after();
                 tc_scale_o(tmem + lane_base + kTcColO, corr);
@@ -653,7 +652,7 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_p0 + 8u * b);
+            if (lane == 0) mbar_arrive(bar_p + 8u * b);
             done = j + 1 == n_kt;
         }
         if (done && tc_warp_wait(bar_last, 0, abort_flag, timeout_ns, err, kDevTimeoutTmemFull)) {
@@ -663,82 +662,115 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
             tmem_ld_32x32b_x32(tmem + lane_base + kTcColO + 32u, r1);
             tmem_ld_32x32b_x16(tmem + lane_base + kTcColO + 64u, r2);
             tmem_ld_wait();
-            if (tid < t.q_rows) {
-                const float l = __uint_as_float(r2[8]);
-                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-                float* dst = out + static_cast<int64_t>(t.o_row0 + tid) * ldo + head * kDH;
+            // Every MMA has completed, so the K buffers are free: stage the
+            // normalised rows there ([128][76] floats: conflict-free 16-byte
+            // stores) and let each warp write its 32 rows whole, 128
+            // contiguous bytes per store instruction.
+            const float l = __uint_as_float(r2[8]);
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const uint32_t row = sK + static_cast<uint32_t>(tid) * kTcOutPitch;
 #pragma unroll
-                for (int d = 0; d < 32; d += 2) {
-                    *reinterpret_cast<float2*>(dst + d) =
-                        make_float2(__uint_as_float(r0[d]) * inv, __uint_as_float(r0[d + 1]) * inv);
-                    *reinterpret_cast<float2*>(dst + 32 + d) =
-                        make_float2(__uint_as_float(r1[d]) * inv, __uint_as_float(r1[d + 1]) * inv);
-                }
+            for (int d = 0; d < 32; d += 4) {
+                sts_v4(row + 4u * d, __float_as_uint(__uint_as_float(r0[d]) * inv),
+                       __float_as_uint(__uint_as_float(r0[d + 1]) * inv),
+                       __float_as_uint(__uint_as_float(r0[d + 2]) * inv),
+                       __float_as_uint(__uint_as_float(r0[d + 3]) * inv));
+                sts_v4(row + 128u + 4u * d, __float_as_uint(__uint_as_float(r1[d]) * inv),
+                       __float_as_uint(__uint_as_float(r1[d + 1]) * inv),
+                       __float_as_uint(__uint_as_float(r1[d + 2]) * inv),
+                       __float_as_uint(__uint_as_float(r1[d + 3]) * inv));
+            }
 #pragma unroll
-                for (int d = 0; d < 8; d += 2)
-                    *reinterpret_cast<float2*>(dst + 64 + d) =
-                        make_float2(__uint_as_float(r2[d]) * inv, __uint_as_float(r2[d + 1]) * inv);
+            for (int d = 0; d < 8; d += 4)
+                sts_v4(row + 256u + 4u * d, __float_as_uint(__uint_as_float(r2[d]) * inv),
+                       __float_as_uint(__uint_as_float(r2[d + 1]) * inv),
+                       __float_as_uint(__uint_as_float(r2[d + 2]) * inv),
+                       __float_as_uint(__uint_as_float(r2[d + 3]) * inv));
+            __syncwarp();
+            const int rows = min(32, t.q_rows - warp * 32);
+            for (int r = 0; r < rows; ++r) {
+                const int rr = warp * 32 + r;
+                float* dst = out + static_cast<int64_t>(t.o_row0 + rr) * ldo + head * kDH;
+                const uint32_t src = sK + static_cast<uint32_t>(rr) * kTcOutPitch;
+                dst[lane] = lds_f32(src + 4u * lane);
+                dst[32 + lane] = lds_f32(src + 128u + 4u * lane);
+                if (lane < 8) dst[64 + lane] = lds_f32(src + 256u + 4u * lane);
             }
         }
-    } else {
-        // ---------------------------------------------------------- control
+    } else if (warp == 4) {
+        // -------------------------------------------------------- MMA issue
         const bool issuer = lane == 0 && !stall;
-        if (issuer) {
-            tc_issue_scores(tmem, sQ, sK);
-            mma_commit(bar_s0);
-            if (n_kt > 1) {
-                tc_issue_scores(tmem + 64u, sQ, sK + kTcKBuf);
-                mma_commit(bar_s1);
-            }
-        }
-        __syncwarp();
-        VStage vs;
-        if (n_kt > 2) tc_fetch_v(vs, vh + static_cast<int64_t>(2 * kKT) * ldv, ldv, min(kKT, t.k_len - 2 * kKT), lane);
-        bool ok = true;
-        if (n_kt > 2) {   // K tile 2 into K buffer 0 once S(0) has read it
-            ok = tc_warp_wait(bar_s0, 0, abort_flag, timeout_ns, err, kDevTimeoutTmemFull);
+        const uint32_t tq = tmem + kTcColQ;
+        bool ok = tc_warp_wait(bar_q, 0, abort_flag, timeout_ns, err, kDevTimeoutFull);
+        for (int j = 0; ok && j < 2 && j < n_kt; ++j) {
+            ok = tc_warp_wait(bar_kf + 8u * j, 0, abort_flag, timeout_ns, err, kDevTimeoutFull);
             if (ok) {
-                tc_load_k(sK, kh + static_cast<int64_t>(2 * kKT) * ldk, ldk, min(kKT, t.k_len - 2 * kKT), lane);
-                cp_async_commit();
+                fence_proxy_async_smem();
+                tc_fence_after();
+                if (issuer) {
+                    tc_issue_scores(tmem + 64u * j, tq, sK + kTcKBuf * j);
+                    mma_commit(bar_s + 8u * j);
+                    mma_commit(bar_ke + 8u * j);
+                }
+                __syncwarp();
             }
         }
+        int b3 = 0, u3 = 0;   // j % 3 and j / 3
         for (int j = 0; ok && j < n_kt; ++j) {
             const uint32_t b = j & 1;
-            if (!tc_warp_wait(bar_p0 + 8u * b, (j >> 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutEmpty)) break;
+            if (!tc_warp_wait(bar_p + 8u * b, (j >> 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutEmpty)) break;
+            if (!tc_warp_wait(bar_vf + 8u * b3, u3 & 1, abort_flag, timeout_ns, err, kDevTimeoutFull)) break;
+            fence_proxy_async_smem();
             tc_fence_after();
             if (issuer) {
-                tc_issue_pv(tmem + kTcColO, tmem + 64u * b, sV + kTcVBuf * b, j > 0);
+                tc_issue_pv(tmem + kTcColO, tmem + 64u * b, sV + kTcVBuf * b3, j > 0);
                 mma_commit(bar_o);
+                mma_commit(bar_ve + 8u * b3);
                 if (j + 1 == n_kt) mma_commit(bar_last);
             }
             __syncwarp();
             if (j + 2 < n_kt) {
-                // P(j) V(j) done: TMEM buffer b and V^T buffer b are free
-                if (!tc_warp_wait(bar_o, j & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull)) break;
+                // S(j+2) overwrites P(j) in TMEM buffer b right behind the
+                // P(j) V(j) that reads it: the tensor core executes one
+                // thread's MMAs in issue order, so no wait is needed; K
+                // tile j+2 must have landed
+                const int b3n = b3 == 0 ? 2 : b3 - 1;               // (j + 2) % 3
+                const int u3n = b3 == 0 ? u3 : u3 + 1;              // (j + 2) / 3
+                if (!tc_warp_wait(bar_kf + 8u * b3n, u3n & 1, abort_flag, timeout_ns, err, kDevTimeoutFull)) break;
+                fence_proxy_async_smem();
                 tc_fence_after();
-                cp_async_wait<0>();   // K tile j+2 (loaded during the previous iteration)
-                fence_proxy_async_smem();
-                __syncwarp();
                 if (issuer) {
-                    tc_issue_scores(tmem + 64u * b, sQ, sK + kTcKBuf * b);
-                    mma_commit(b ? bar_s1 : bar_s0);
+                    tc_issue_scores(tmem + 64u * b, tq, sK + kTcKBuf * b3n);
+                    mma_commit(bar_s + 8u * b);
+                    mma_commit(bar_ke + 8u * b3n);
                 }
-                tc_store_vt(vs, sV + kTcVBuf * b, lane);
-                fence_proxy_async_smem();
                 __syncwarp();
-                if (j + 3 < n_kt) {
-                    const int k0 = (j + 3) * kKT;
-                    tc_fetch_v(vs, vh + static_cast<int64_t>(k0) * ldv, ldv, min(kKT, t.k_len - k0), lane);
-                }
             }
-            if (j + 3 < n_kt) {   // K tile j+3 into K buffer (j+1) % 2 once S(j+1) has read it
-                const uint32_t b1 = b ^ 1u;
-                if (!tc_warp_wait(b1 ? bar_s1 : bar_s0, ((j + 1) >> 1) & 1, abort_flag, timeout_ns, err,
-                                  kDevTimeoutTmemFull))
-                    break;
-                const int k0 = (j + 3) * kKT;
-                tc_load_k(sK + kTcKBuf * b1, kh + static_cast<int64_t>(k0) * ldk, ldk, min(kKT, t.k_len - k0), lane);
-                cp_async_commit();
+            if (++b3 == kTcStages) {
+                b3 = 0;
+                ++u3;
+            }
+        }
+    } else {
+        // ----------------------------------------------------------- loader
+        // k_full / v_full [j % 3] phase j / 3 carries tile j; k_empty /
+        // v_empty [j % 3] phase j / 3 is S(j) / P(j) V(j)
+        for (int j = 0; j < kTcStages && j < n_kt; ++j) {
+            cp_async_arrive_noinc(bar_kf + 8u * j);
+            cp_async_arrive_noinc(bar_vf + 8u * j);
+        }
+        int b3 = 0, u3 = 0;   // (j - 3) % 3 == j % 3 and (j - 3) / 3
+        for (int j = kTcStages; j < n_kt; ++j) {
+            const int k0 = j * kKT, valid = min(kKT, t.k_len - k0);
+            if (!tc_warp_wait(bar_ke + 8u * b3, u3 & 1, abort_flag, timeout_ns, err, kDevTimeoutEmpty)) break;
+            tc_load_tile(sK + kTcKBuf * b3, kh + static_cast<int64_t>(k0) * ldk, ldk, valid, lane);
+            cp_async_arrive_noinc(bar_kf + 8u * b3);
+            if (!tc_warp_wait(bar_ve + 8u * b3, u3 & 1, abort_flag, timeout_ns, err, kDevTimeoutEmpty)) break;
+            tc_load_tile(sV + kTcVBuf * b3, vh + static_cast<int64_t>(k0) * ldv, ldv, valid, lane);
+            cp_async_arrive_noinc(bar_vf + 8u * b3);
+            if (++b3 == kTcStages) {
+                b3 = 0;
+                ++u3;
             }
         }
     }
@@ -751,7 +783,7 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     tmem_st_wait();
     tc_fence_before();
     __syncthreads();
-    if (tid == 128) {
+    if (tid == 128) {   // the MMA issuer
         tc_fence_after();
         mma_commit(bar_fin);
         volatile uint32_t no_abort = 0;

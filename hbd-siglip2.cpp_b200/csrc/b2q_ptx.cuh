@@ -171,7 +171,23 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptors (dense, both operands K-major).
+// Shared-memory matrix descriptor, MN-major operand with the 128-byte swizzle:
+// rows of 64 MN-consecutive 16-bit elements (128 bytes) per K index, 8 K rows
+// per 1024-byte atom (stride-dimension offset 1024 B), the next 64 MN
+// elements `lbo_bytes` further on (leading-dimension offset).
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(2u) << 61;
+    return d;
+}
+
+// Instruction descriptors (dense, both operands K-major; OR in kIdescBMajorMN
+// for an MN-major B).
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
 __host__ __device__ constexpr uint32_t idesc_i8_s32(uint32_t M, uint32_t N) {
     return (2u << 4)            // D: s32
            | (1u << 7)          // A: signed 8-bit
@@ -215,6 +231,12 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uin
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
         "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+// Arrive on `bar` (counting as one of its expected arrivals) once every
+// cp.async this thread issued so far has completed.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 // Arrive on `bar` once every tcgen05 op this thread issued so far completes.
