@@ -227,6 +227,38 @@ def profile_gemm(tokens):
     return 0
 
 
+def profile_attention(n_images):
+    """Time one layer's attention over a packed batch of n_images NaFlex images
+    (the bench's seeded grids, random fp16 [Q|K|V] rows) with each tensor-core
+    kernel; CUDA events.  Algorithmic work 4*L^2*72 flops per head."""
+    import torch
+    import b2q
+    from b2q import synth
+    b2q.init(0)
+    cfg = synth.TowerConfig()
+    H, nh = cfg.hidden, cfg.n_head
+    grids = synth.naflex_grids(n_images, seed=0)
+    lens = [int(h) * int(w) for h, w in grids]
+    offs = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    T = int(sum(lens))
+    qkv = torch.randn((T, 3 * H), device="cuda", dtype=torch.float16)
+    out = torch.empty((T, H), device="cuda", dtype=torch.float32)
+    flops = sum(4.0 * L * L * (H // nh) * nh for L in lens)
+
+    def run():
+        b2q.attention(qkv, 3 * H, qkv[:, H:], 3 * H, qkv[:, 2 * H:], 3 * H, offs, lens, offs, lens, offs, nh, out, H)
+
+    res = {"kernel": "attention", "images": n_images, "tokens": T}
+    for name, k in (("tcgen05", 0), ("mma_sync", 1)):
+        b2q.tune(b2q.TUNE_ATTN_KERNEL, k)
+        ms = min(_events_ms(run, 1) for _ in range(5))
+        res[name] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12}
+    b2q.tune(b2q.TUNE_ATTN_KERNEL, 0)
+    b2q.check_device()
+    print(json.dumps(res), flush=True)
+    return 0
+
+
 def _events_ms(fn, reps, warm=2):
     import torch
     for _ in range(warm):
@@ -355,6 +387,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="TOKENS",
                     help="only run the fc1 GEMM (GELU->q8_1 epilogue) at this token count, for ncu captures")
+    ap.add_argument("--profile-attention", type=int, default=0, metavar="IMAGES",
+                    help="only time one layer's attention over this many NaFlex images, both tensor-core kernels")
     ap.add_argument("--suite", action="store_true", help="configs 1, 2, 3 and 5 on one GPU (JSON lines)")
     ap.add_argument("--out", default="", help="--suite: also write the JSON lines to this file")
     args = ap.parse_args()
@@ -362,6 +396,8 @@ def main():
         return reference_arm(args)
     if args.profile_gemm:
         return profile_gemm(args.profile_gemm)
+    if args.profile_attention:
+        return profile_attention(args.profile_attention)
     if args.suite:
         return suite(args)
 
