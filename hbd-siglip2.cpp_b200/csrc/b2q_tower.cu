@@ -16,6 +16,7 @@
 // (build_probe_head, src/siglip2_vision.cpp:249-314).
 #include "b2q_tower.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -59,31 +60,52 @@ __device__ __forceinline__ int aa_taps(int in, int out, int i, int* lo, double* 
     return n;
 }
 
-__global__ void pos_resize_kernel(const float* __restrict__ table, int side, int H, const ImageDesc* __restrict__ imgs,
-                                  float* __restrict__ out) {
+// One block per kPosTok tokens of one image: the block's first threads
+// compute each token's row and column taps once (shared memory), then all
+// threads sweep the H channels, so the taps (double divisions) are not
+// recomputed per channel and the table and output rows are read and written
+// contiguously.  The per-element arithmetic and its order are those of the
+// filter definition above.
+constexpr int kPosTok = 8;
+constexpr int kPosMaxTaps = 64;
+
+__global__ void __launch_bounds__(128) pos_resize_kernel(const float* __restrict__ table, int side, int H,
+                                                         const ImageDesc* __restrict__ imgs, float* __restrict__ out) {
+    __shared__ double s_wy[kPosTok][kPosMaxTaps], s_wx[kPosTok][kPosMaxTaps];
+    __shared__ int s_ny[kPosTok], s_nx[kPosTok], s_ly[kPosTok], s_lx[kPosTok];
     const ImageDesc im = imgs[blockIdx.y];
     const int n_tok = im.h * im.w;
-    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n_tok * H; idx += gridDim.x * blockDim.x) {
-        const int t = idx / H, i = idx % H;
-        const int r = t / im.w, c = t % im.w;
-        float v;
-        if (im.h == side && im.w == side) {
-            v = table[static_cast<int64_t>(t) * H + i];
-        } else {
-            double wy[64], wx[64];
-            int ly, lx;
-            const int ny = aa_taps(side, im.h, r, &ly, wy);
-            const int nx = aa_taps(side, im.w, c, &lx, wx);
+    const int t_base = blockIdx.x * kPosTok;
+    if (t_base >= n_tok) return;
+    const bool same = im.h == side && im.w == side;
+    if (!same && threadIdx.x < 2 * kPosTok) {
+        const int k = threadIdx.x >> 1, t = t_base + k;
+        if (t < n_tok) {
+            if (threadIdx.x & 1)
+                s_nx[k] = aa_taps(side, im.w, t % im.w, &s_lx[k], s_wx[k]);
+            else
+                s_ny[k] = aa_taps(side, im.h, t / im.w, &s_ly[k], s_wy[k]);
+        }
+    }
+    __syncthreads();
+    for (int k = 0; k < kPosTok && t_base + k < n_tok; ++k) {
+        const int t = t_base + k;
+        float* dst = out + static_cast<int64_t>(im.t0 + t) * H;
+        if (same) {
+            for (int i = threadIdx.x; i < H; i += blockDim.x) dst[i] = table[static_cast<int64_t>(t) * H + i];
+            continue;
+        }
+        const int ny = s_ny[k], nx = s_nx[k], ly = s_ly[k], lx = s_lx[k];
+        for (int i = threadIdx.x; i < H; i += blockDim.x) {
             double acc = 0.0;
             for (int a = 0; a < ny; ++a) {
                 double row = 0.0;
                 for (int b = 0; b < nx; ++b)
-                    row = __dadd_rn(row, __dmul_rn(wx[b], table[static_cast<int64_t>((ly + a) * side + lx + b) * H + i]));
-                acc = __dadd_rn(acc, __dmul_rn(wy[a], static_cast<double>(static_cast<float>(row))));
+                    row = __dadd_rn(row, __dmul_rn(s_wx[k][b], table[static_cast<int64_t>((ly + a) * side + lx + b) * H + i]));
+                acc = __dadd_rn(acc, __dmul_rn(s_wy[k][a], static_cast<double>(static_cast<float>(row))));
             }
-            v = static_cast<float>(acc);
+            dst[i] = static_cast<float>(acc);
         }
-        out[static_cast<int64_t>(im.t0 + t) * H + i] = v;
     }
 }
 
@@ -231,8 +253,10 @@ b2q_status b2q_vision_create(const b2q_vision_config* cfg, b2q_vision** out) {
     (void) ds;
     if (!cfg || !out) return set_error(B2Q_ERR_INVALID, "null pointer");
     if (cfg->hidden != cfg->n_head * 72 || cfg->hidden % 128 || cfg->hidden / 128 != 9 || cfg->ffn <= 0 ||
-        cfg->n_layer <= 0 || cfg->patch_dim % 32 || cfg->pos_side <= 0)
-        return set_error(B2Q_ERR_SHAPE, "vision config: needs hidden 1152 = 16 heads x 72, patch_dim % 32 == 0");
+        cfg->n_layer <= 0 || cfg->patch_dim % 32 || cfg->pos_side <= 0 ||
+        cfg->pos_side > kPosMaxTaps)   // a resize tap count is at most the table side
+        return set_error(B2Q_ERR_SHAPE,
+                         "vision config: needs hidden 1152 = 16 heads x 72, patch_dim % 32 == 0, pos_side in 1..64");
     b2q_vision* v = new b2q_vision();
     v->cfg = *cfg;
     v->ffn_pad = static_cast<int>(round_up(cfg->ffn, 32));
@@ -358,9 +382,10 @@ b2q_status b2q_vision_encode(b2q_vision* v, const float* patches, const int32_t*
 
     // ---- stem: x = (patches . W + b) + pos  (src/siglip2_vision.cpp:676-691) ----
     {
-        dim3 grid(static_cast<unsigned>((1024 * H + 255) / 256 < 4096 ? (1024 * H + 255) / 256 : 4096),
-                  static_cast<unsigned>(n_images));
-        pos_resize_kernel<<<grid, 256, 0, s>>>(v->f("v.position_embd.weight"), c.pos_side, static_cast<int>(H),
+        int max_tok = 1;
+        for (int i = 0; i < n_images; ++i) max_tok = std::max(max_tok, grid_hw[2 * i] * grid_hw[2 * i + 1]);
+        dim3 grid(static_cast<unsigned>((max_tok + kPosTok - 1) / kPosTok), static_cast<unsigned>(n_images));
+        pos_resize_kernel<<<grid, 128, 0, s>>>(v->f("v.position_embd.weight"), c.pos_side, static_cast<int>(H),
                                               v->imgs.as<ImageDesc>(), pos);
         count_launch();
         B2Q_TRY(cuda_check(cudaGetLastError(), "pos resize launch"));
