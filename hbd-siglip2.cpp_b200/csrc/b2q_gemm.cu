@@ -224,53 +224,88 @@ __device__ bool run_mma(const Smem& sm, uint32_t tmem_base, const GemmParams& p,
 // columns) makes each shared-memory scale load serve four rows, which keeps
 // the per-block rescale off the shared-memory pipe.
 
+constexpr int kResBatch = 4;   // column groups (of 8) per batch of residual loads in store_tile
+
 template <int kOps, int kBN>
 __device__ __forceinline__ void store_tile(const GemmParams& p, float2* acc, int mrow0, int nblk0, int q) {
     using Cfg = GemmCfg<kOps, kBN>;
     if (p.epi == B2Q_EPI_BIAS_GELU_Q8) {
+        // In phases over the whole tile, so that the independent element
+        // chains overlap: bias + GELU in place for all 64 pairs, then each
+        // (row, 32-column block)'s absmax and scales, then rounding and
+        // stores.  Per element the operations are those of the q8_1 rule.
+#pragma unroll
+        for (int cc = 0; cc < Cfg::CC; ++cc)
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                const int n = nblk0 + cc * 64 + 8 * g + 2 * q;
+                const float2 b = (p.bias && n < p.N) ? *reinterpret_cast<const float2*>(p.bias + n) : make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int s = 0; s < 2; ++s)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float2& a = acc[16 * (2 * cc + s) + 2 * g + h];
+                        a = gelu2(__fadd2_rn(a, b));
+                    }
+            }
+        // absmax of each (row, block): this thread's 8 values, then the 4 lanes sharing t/4
+        float amax[Cfg::CC][2][2][2];
+#pragma unroll
+        for (int cc = 0; cc < Cfg::CC; ++cc)
+#pragma unroll
+            for (int bl = 0; bl < 2; ++bl)
+#pragma unroll
+                for (int s = 0; s < 2; ++s)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float m = 0.0f;
+#pragma unroll
+                        for (int gg = 0; gg < 4; ++gg) {
+                            const float2 v = acc[16 * (2 * cc + s) + 2 * (4 * bl + gg) + h];
+                            m = fmaxf(m, fmaxf(fabsf(v.x), fabsf(v.y)));
+                        }
+                        amax[cc][bl][s][h] = m;
+                    }
+#pragma unroll
+        for (int cc = 0; cc < Cfg::CC; ++cc)
+#pragma unroll
+            for (int bl = 0; bl < 2; ++bl)
+#pragma unroll
+                for (int s = 0; s < 2; ++s)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float& m = amax[cc][bl][s][h];
+                        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+                        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+                    }
 #pragma unroll
         for (int cc = 0; cc < Cfg::CC; ++cc) {
 #pragma unroll
             for (int bl = 0; bl < 2; ++bl) {
                 const int n0 = nblk0 + cc * 64 + bl * 32;        // q8_1 block start (warp-uniform)
                 if (n0 >= p.Kp_out) continue;
-                float2 b2[4];
-#pragma unroll
-                for (int gg = 0; gg < 4; ++gg) {
-                    const int n = n0 + 8 * gg + 2 * q;
-                    b2[gg] = (p.bias && n < p.N) ? *reinterpret_cast<const float2*>(p.bias + n) : make_float2(0.0f, 0.0f);
-                }
 #pragma unroll
                 for (int s = 0; s < 2; ++s) {
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        float2 v[4];
-                        float amax = 0.0f;
+                        const int m = mrow0 + 16 * s + 8 * h;
+                        if (m >= p.M) continue;
+                        const float a = amax[cc][bl][s][h];
+                        if (q == 0) p.d_out[static_cast<int64_t>(n0 / 32) * p.d_ld + m] = q8_scale(a);
+                        const float inv = q8_inv_scale(a);
 #pragma unroll
                         for (int gg = 0; gg < 4; ++gg) {
-                            v[gg] = gelu2(__fadd2_rn(acc[16 * (2 * cc + s) + 2 * (4 * bl + gg) + h], b2[gg]));
-                            amax = fmaxf(amax, fmaxf(fabsf(v[gg].x), fabsf(v[gg].y)));
-                        }
-                        // the block's 32 values of this row sit in the 4 lanes sharing t/4
-                        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-                        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-                        const int m = mrow0 + 16 * s + 8 * h;
-                        if (m < p.M) {
-                            if (q == 0) p.d_out[static_cast<int64_t>(n0 / 32) * p.d_ld + m] = q8_scale(amax);
-                            const float inv = q8_inv_scale(amax);
-#pragma unroll
-                            for (int gg = 0; gg < 4; ++gg) {
-                                const int64_t off = static_cast<int64_t>(m) * p.Kp_out + n0 + 8 * gg + 2 * q;
-                                if constexpr (kOps == kOpsF16) {
-                                    reinterpret_cast<__half2*>(reinterpret_cast<__half*>(p.q_out) + off)[0] =
-                                        __halves2half2(__int2half_rn(q8_round(v[gg].x, inv)),
-                                                       __int2half_rn(q8_round(v[gg].y, inv)));
-                                } else {
-                                    const uint32_t lo = static_cast<uint32_t>(q8_round(v[gg].x, inv)) & 0xFFu;
-                                    const uint32_t hi = static_cast<uint32_t>(q8_round(v[gg].y, inv)) & 0xFFu;
-                                    reinterpret_cast<uint16_t*>(reinterpret_cast<int8_t*>(p.q_out) + off)[0] =
-                                        static_cast<uint16_t>(lo | (hi << 8));
-                                }
+                            const float2 v = acc[16 * (2 * cc + s) + 2 * (4 * bl + gg) + h];
+                            const int64_t off = static_cast<int64_t>(m) * p.Kp_out + n0 + 8 * gg + 2 * q;
+                            const int32_t q0 = q8_round(v.x, inv), q1 = q8_round(v.y, inv);
+                            if constexpr (kOps == kOpsF16) {
+                                reinterpret_cast<__half2*>(reinterpret_cast<__half*>(p.q_out) + off)[0] =
+                                    __halves2half2(__int2half_rn(q0), __int2half_rn(q1));
+                            } else {
+                                const uint32_t lo = static_cast<uint32_t>(q0) & 0xFFu;
+                                const uint32_t hi = static_cast<uint32_t>(q1) & 0xFFu;
+                                reinterpret_cast<uint16_t*>(reinterpret_cast<int8_t*>(p.q_out) + off)[0] =
+                                    static_cast<uint16_t>(lo | (hi << 8));
                             }
                         }
                     }
@@ -302,31 +337,52 @@ __device__ __forceinline__ void store_tile(const GemmParams& p, float2* acc, int
     } else {
         float* out = reinterpret_cast<float*>(p.out);
         const bool add_bias = p.epi != B2Q_EPI_NONE && p.bias;
+        const bool add_res = p.epi == B2Q_EPI_BIAS_RESIDUAL;
+        // In batches of kResBatch column groups: the batch's residual values are all
+        // loaded before any of its outputs is stored.  Each thread reads
+        // exactly the elements it writes (the residual may be the output
+        // itself), so the early loads are safe, and one memory latency per
+        // batch replaces one per element pair.
 #pragma unroll
         for (int cc = 0; cc < Cfg::CC; ++cc) {
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-                const int n = nblk0 + cc * 64 + 8 * g + 2 * q;
-                if (n >= p.N) continue;
-                const float2 b = add_bias ? *reinterpret_cast<const float2*>(p.bias + n) : make_float2(0.0f, 0.0f);
+            for (int g0 = 0; g0 < 8; g0 += kResBatch) {
+                float2 r[kResBatch][2][2];
 #pragma unroll
-                for (int s = 0; s < 2; ++s) {
+                for (int g = 0; g < kResBatch; ++g)
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int m = mrow0 + 16 * s + 8 * h;
-                        if (m >= p.M) continue;
-                        float2 v = acc[16 * (2 * cc + s) + 2 * g + h];
-                        if (add_bias) {
-                            v.x = __fadd_rn(v.x, b.x);
-                            v.y = __fadd_rn(v.y, b.y);
+                    for (int s = 0; s < 2; ++s)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int n = nblk0 + cc * 64 + 8 * (g0 + g) + 2 * q;
+                            const int m = mrow0 + 16 * s + 8 * h;
+                            r[g][s][h] = (add_res && n < p.N && m < p.M)
+                                             ? *reinterpret_cast<const float2*>(p.residual +
+                                                                                static_cast<int64_t>(m) * p.ld_out + n)
+                                             : make_float2(0.0f, 0.0f);
                         }
-                        const int64_t off = static_cast<int64_t>(m) * p.ld_out + n;
-                        if (p.epi == B2Q_EPI_BIAS_RESIDUAL) {
-                            const float2 r = *reinterpret_cast<const float2*>(p.residual + off);
-                            v.x = __fadd_rn(v.x, r.x);
-                            v.y = __fadd_rn(v.y, r.y);
+#pragma unroll
+                for (int g = 0; g < kResBatch; ++g) {
+                    const int n = nblk0 + cc * 64 + 8 * (g0 + g) + 2 * q;
+                    if (n >= p.N) continue;
+                    const float2 b = add_bias ? *reinterpret_cast<const float2*>(p.bias + n) : make_float2(0.0f, 0.0f);
+#pragma unroll
+                    for (int s = 0; s < 2; ++s) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int m = mrow0 + 16 * s + 8 * h;
+                            if (m >= p.M) continue;
+                            float2 v = acc[16 * (2 * cc + s) + 2 * (g0 + g) + h];
+                            if (add_bias) {
+                                v.x = __fadd_rn(v.x, b.x);
+                                v.y = __fadd_rn(v.y, b.y);
+                            }
+                            if (add_res) {
+                                v.x = __fadd_rn(v.x, r[g][s][h].x);
+                                v.y = __fadd_rn(v.y, r[g][s][h].y);
+                            }
+                            *reinterpret_cast<float2*>(out + static_cast<int64_t>(m) * p.ld_out + n) = v;
                         }
-                        *reinterpret_cast<float2*>(out + off) = v;
                     }
                 }
             }

@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 
 namespace b2q {
 
@@ -51,6 +52,19 @@ __device__ __forceinline__ float2 own_div2(float2 a, float2 b) {
     return __ffma2_rn(__ffma2_rn(nb, q0, a), y, q0);
 }
 
+// Round to nearest even of |t| < 2^22 on the fp32 adder: t + 1.5*2^23 lands
+// in [2^23, 2^24), where the ulp is 1, so the addition itself rounds t to an
+// integer; subtracting the constant again is exact, and the integer is the
+// difference of the bit patterns.  Identical to rintf / __float2int_rn on
+// that range, without the conversion pipe.
+constexpr float kRintMagic = 12582912.0f;   // 1.5 * 2^23, bits 0x4B400000
+__device__ __forceinline__ float2 rint2_adder(float2 t, int32_t& n0, int32_t& n1) {
+    const float2 tm = __fadd2_rn(t, make_float2(kRintMagic, kRintMagic));
+    n0 = __float_as_int(tm.x) - 0x4B400000;
+    n1 = __float_as_int(tm.y) - 0x4B400000;
+    return __fadd2_rn(tm, make_float2(-kRintMagic, -kRintMagic));
+}
+
 __device__ __forceinline__ float2 gelu2(float2 x) {
     const float2 x2 = __fmul2_rn(x, x);
     const float2 inner = __ffma2_rn(make_float2(0.044715f, 0.044715f), x2, make_float2(1.0f, 1.0f));
@@ -60,7 +74,8 @@ __device__ __forceinline__ float2 gelu2(float2 x) {
     z.y = fminf(fmaxf(z.y, -80.0f), 80.0f);
     // e^z, as own_expf
     const float2 t = __fmul2_rn(z, make_float2(1.44269504088896340736f, 1.44269504088896340736f));
-    const float2 n = make_float2(rintf(t.x), rintf(t.y));
+    int32_t n0, n1;   // |t| <= 80 * log2(e)
+    const float2 n = rint2_adder(t, n0, n1);
     float2 r = __ffma2_rn(n, make_float2(-0.693145751953125f, -0.693145751953125f), z);
     r = __ffma2_rn(n, make_float2(-1.42860682030941723212e-6f, -1.42860682030941723212e-6f), r);
     const float kc[9] = {2.48015873015873015873e-5f, 1.98412698412698412698e-4f, 1.38888888888888888889e-3f,
@@ -69,8 +84,7 @@ __device__ __forceinline__ float2 gelu2(float2 x) {
     float2 p = make_float2(kc[0], kc[0]);
 #pragma unroll
     for (int i = 1; i < 9; ++i) p = __ffma2_rn(p, r, make_float2(kc[i], kc[i]));
-    const float2 sc = make_float2(__int_as_float((static_cast<int32_t>(n.x) + 127) << 23),
-                                  __int_as_float((static_cast<int32_t>(n.y) + 127) << 23));
+    const float2 sc = make_float2(__int_as_float((n0 + 127) << 23), __int_as_float((n1 + 127) << 23));
     const float2 d = __fadd2_rn(make_float2(1.0f, 1.0f), __fmul2_rn(p, sc));
     return own_div2(x, d);
 }
