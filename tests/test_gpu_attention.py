@@ -40,7 +40,7 @@ def check_close(out, ref):
     assert cos.min() >= 0.99999, cos.min()
 
 
-@pytest.mark.parametrize("lens", [[1], [7], [64, 65], [127, 128, 129], [729], [1, 5, 100, 256, 1024]])
+@pytest.mark.parametrize("lens", [[1], [7], [64, 65], [127, 128, 129], [729], [1, 5, 100, 256, 1024], [3000]])
 def test_self_attention_varlen(oracle, kernel, lens):
     rng = np.random.default_rng(len(lens) * 1000 + sum(lens))
     T = sum(lens)
