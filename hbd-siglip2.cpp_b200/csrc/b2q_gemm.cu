@@ -63,6 +63,7 @@ struct GemmCfg {
 struct GemmParams {
     int M, N, Kb;
     int m_tiles, n_tiles;
+    int nb_off;         // first column tile of this launch (tiles cover columns (nb_off + nb) * BN)
     int epi;
     const float* bias;
     const float* residual;
@@ -144,7 +145,7 @@ __device__ bool run_producer(const Smem& sm, const CUtensorMap* tmA, const CUten
     if (p.stall) return true;   // nothing issued: the consumers' bounded waits run out
     Ring<Cfg::STAGES> st_ring;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles;
+        const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles + p.nb_off;
         for (int st = 0; st < nst; ++st) {
             const uint32_t s = st_ring.idx;
             if (!mbar_wait(bar_at(sm.empty, s), st_ring.phase ^ 1u, sm.abort_flag, p.timeout_ns)) {
@@ -404,7 +405,7 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
     Ring<Cfg::STAGES> st_ring;
     Ring<Cfg::NBUF> acc_ring;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles;
+        const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles + p.nb_off;
         const int mrow0 = mb * Cfg::BM + rloc;
         const int nblk0 = nb * Cfg::BN + col0;
         float2 acc[Cfg::COLS / 2];
@@ -614,8 +615,10 @@ static cudaError_t configure_once() {
     return e;
 }
 
+// Output columns [n_base, n_base + n_cols) of the GEMM, in kBN-column tiles
+// (n_base a multiple of kBN).
 template <int kOps, int kBN, bool kDump>
-static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s) {
+static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s, int64_t n_base, int64_t n_cols) {
     using Cfg = GemmCfg<kOps, kBN>;
     DeviceState* ds = state();
     const b2q_weight* w = a.w;
@@ -635,7 +638,8 @@ static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s) {
     p.N = static_cast<int>(w->N);
     p.Kb = static_cast<int>(w->Kb);
     p.m_tiles = static_cast<int>((a.M + Cfg::BM - 1) / Cfg::BM);
-    p.n_tiles = static_cast<int>((w->N + Cfg::BN - 1) / Cfg::BN);
+    p.n_tiles = static_cast<int>((n_cols + Cfg::BN - 1) / Cfg::BN);
+    p.nb_off = static_cast<int>(n_base / Cfg::BN);
     p.epi = a.epi;
     p.bias = a.bias;
     p.residual = a.residual;
@@ -661,28 +665,50 @@ static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s) {
     return cuda_check(cudaGetLastError(), "gemm launch");
 }
 
+// 256-column tiles leave the last tile of N part empty when N is not a
+// multiple of 256 (N = 1152: five tiles for 4.5 tiles of work, and the
+// epilogue costs the same for the empty half).  When the remainder fits one
+// 128-column tile, the columns are covered by two launches instead: 256-wide
+// tiles up to the last multiple of 256, then 128-wide tiles for the rest.
+// Every output element is computed exactly as in a single launch.
+static int64_t split_remainder(int64_t N) {
+    const int64_t rem = N % 256;
+    return (N > 256 && rem != 0 && rem <= 128) ? rem : 0;
+}
+
 template <int kOps>
-static b2q_status dispatch_bn(const GemmArgs& a, cudaStream_t s, int bn) {
-    if (a.dump) return run_gemm<kOps, 128, true>(a, s);
-    return bn == 256 ? run_gemm<kOps, 256, false>(a, s) : run_gemm<kOps, 128, false>(a, s);
+static b2q_status dispatch_bn(const GemmArgs& a, cudaStream_t s, int bn, bool split) {
+    const int64_t N = a.w->N;
+    if (a.dump) return run_gemm<kOps, 128, true>(a, s, 0, N);
+    if (bn != 256) return run_gemm<kOps, 128, false>(a, s, 0, N);
+    const int64_t rem = split ? split_remainder(N) : 0;
+    if (rem == 0) return run_gemm<kOps, 256, false>(a, s, 0, N);
+    b2q_status st = run_gemm<kOps, 256, false>(a, s, 0, N - rem);
+    if (st != B2Q_OK) return st;
+    return run_gemm<kOps, 128, false>(a, s, N - rem, rem);
 }
 
 // Tile width when not forced by B2Q_TUNE_GEMM_BN: whichever of 256 and 128
 // columns finishes the persistent grid's tile rounds sooner, with a
 // 128-column tile costing about 0.6 of a 256-column one (it carries the same
-// per-K-block synchronisation for half the columns).  Large M keeps 256;
-// small M (few tiles, or a last round that is mostly empty) takes 128.
+// per-K-block synchronisation for half the columns), and the 256 option
+// counting its split remainder launch.  Large M keeps 256; small M (few
+// tiles, or a last round that is mostly empty) takes 128.
 static int auto_bn(int64_t M, int64_t N, int num_sms) {
     const int64_t mt = (M + 127) / 128;
-    const int64_t r256 = (mt * ((N + 255) / 256) + num_sms - 1) / num_sms;
+    const int64_t rem = split_remainder(N);
+    const double r256 = rem ? static_cast<double>((mt * (N / 256) + num_sms - 1) / num_sms) +
+                                  0.6 * static_cast<double>((mt + num_sms - 1) / num_sms)
+                            : static_cast<double>((mt * ((N + 255) / 256) + num_sms - 1) / num_sms);
     const int64_t r128 = (mt * ((N + 127) / 128) + num_sms - 1) / num_sms;
-    return 0.6 * static_cast<double>(r128) < 0.95 * static_cast<double>(r256) ? 128 : 256;
+    return 0.6 * static_cast<double>(r128) < 0.95 * r256 ? 128 : 256;
 }
 
 b2q_status launch_gemm(const GemmArgs& a, cudaStream_t s) {
     DeviceState* ds = state();
-    const int bn = ds->gemm_bn == 128 ? 128 : ds->gemm_bn == 256 ? 256 : auto_bn(a.M, a.w->N, ds->num_sms);
-    return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, bn) : dispatch_bn<kOpsI8>(a, s, bn);
+    const bool forced = ds->gemm_bn == 128 || ds->gemm_bn == 256;
+    const int bn = forced ? ds->gemm_bn : auto_bn(a.M, a.w->N, ds->num_sms);
+    return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, bn, !forced) : dispatch_bn<kOpsI8>(a, s, bn, !forced);
 }
 
 // Weight tensor maps are built once at registration (box = 128 bytes of K by

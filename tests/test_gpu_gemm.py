@@ -199,6 +199,39 @@ def test_full_size_sampled_rows(oracle, mode):
     np.testing.assert_array_equal(y[torch.from_numpy(rows).cuda()].cpu().numpy(), oracle.gemm_q8(w_q, N, K, qs, dx))
 
 
+@pytest.mark.parametrize("N,kind", [(1152, "residual"), (3456, "f16")])
+def test_large_m_column_split(oracle, mode, N, kind):
+    # At this M the automatic tile choice covers N = 1152 / 3456 with
+    # 256-column tiles up to the last multiple of 256 and a second launch of
+    # 128-column tiles for the remaining 128 columns; sampled rows are checked
+    # bit-exactly over every column, the seam at 1024 / 3328 included.
+    M, K = 40000, 1152
+    w_q = synth.quantize_q8_0(rand((N, K), 31, 0.02))
+    bias = rand(N, 32, 0.1)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn((M, K), generator=g, device="cuda")
+    W = b2q.Weight(w_q, N, K)
+    act = b2q.act_empty(M, K)
+    b2q.quantize_q8_1(x, act, M, K)
+    rows = np.concatenate([np.arange(0, 130), np.random.default_rng(1).integers(0, M, 200), np.arange(M - 130, M)])
+    idx = torch.from_numpy(rows).cuda()
+    qs, dx = oracle.quantize_q8_1(x[idx].cpu().numpy())
+    acc = oracle.gemm_q8(w_q, N, K, qs, dx)
+    if kind == "residual":
+        res = torch.randn((M, N), generator=g, device="cuda")
+        ref = (acc + bias) + res[idx].cpu().numpy()
+        y = res   # in place, as the towers run it
+        b2q.mul_mat(W, act, M, y, kind=b2q.EPI_BIAS_RESIDUAL, bias=dev(bias), residual=y)
+    else:
+        ref = (acc + bias).astype(np.float16)
+        y = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        b2q.mul_mat(W, act, M, y, kind=b2q.EPI_BIAS_F16, bias=dev(bias))
+    torch.cuda.synchronize()
+    assert b2q.check_device() == 0
+    np.testing.assert_array_equal(y[idx].cpu().numpy(), ref)
+    W.release()
+
+
 def test_bad_arguments_return_status(mode):
     W = b2q.Weight(synth.quantize_q8_0(rand((16, 64), 1)), 16, 64)
     act = b2q.act_empty(4, 64)
