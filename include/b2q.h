@@ -176,7 +176,9 @@ b2q_status b2q_block_sums(const b2q_weight *w, const void *act, int64_t M, int32
  * query rows from q_off[s], k_len[s] keys/values from k_off[s], and writes
  * out[o_off[s] + i][h*72 + d] (fp32, row stride ldo).  Softmax scale
  * 1/sqrt(72).  tiles_scratch: device memory of b2q_attention_scratch_bytes()
- * for the same sequence description (the tile table is copied into it). */
+ * for the same sequence description (the tile table is copied into it).
+ * Runs on the tcgen05 kernel unless B2Q_TUNE_ATTN_KERNEL (mma.sync) or
+ * B2Q_TUNE_ATTN_EXACT (fixed fp32 order) selects another. */
 size_t b2q_attention_scratch_bytes(const int32_t *q_len, int32_t n_seq);
 b2q_status b2q_attention(const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v, int64_t ldv,
                          const int32_t *q_off, const int32_t *q_len, const int32_t *k_off, const int32_t *k_len,
