@@ -353,11 +353,11 @@ attention_exact_kernel(const __half* __restrict__ q, int64_t ldq, const __half* 
 // the output accumulator O (80 columns; column 72 = running row sum) at
 // column 128; Q (the A operand of the scores: 80 dims as fp16 pairs, dims
 // 72..79 zero) at column 208.
-constexpr int kTcThreads = 192;   // warps 0-3: softmax (one query row each), 4: MMA issue, 5: loads
+constexpr int kTcThreads = 224;   // warps 0-3: softmax (one query row each), 4: P V issue, 5: loads, 6: score issue
 constexpr int kTcStages = 3;
 constexpr uint32_t kTcK = 0, kTcKBuf = 16384, kTcV = 49152, kTcVBuf = 16384;
 constexpr uint32_t kTcBar = 98304;
-constexpr int kTcSmem = static_cast<int>(kTcBar) + 192 + 1024;   // 20 barriers, TMEM slot, abort flag
+constexpr int kTcSmem = static_cast<int>(kTcBar) + 192 + 1024;   // 21 barriers, TMEM slot, abort flag
 constexpr uint32_t kTcTmemCols = 256, kTcColO = 128, kTcColQ = 208;
 constexpr uint32_t kTcOutPitch = 304;   // bytes per staged output row (76 floats)
 
@@ -442,22 +442,18 @@ __device__ __forceinline__ bool tc_warp_wait(uint32_t bar, uint32_t parity, vola
     return __all_sync(0xffffffffu, ok);
 }
 
-// Multiplies this thread's row of O (80 columns) in TMEM by f.
+// Multiplies this thread's row of O (80 columns) in TMEM by f, 16 columns
+// at a time (the row's 64 scores stay live in registers meanwhile).
 __device__ __forceinline__ void tc_scale_o(uint32_t taddr, float f) {
-    uint32_t r[32], r2[16];
+    uint32_t r[16];
 #pragma unroll
-    for (uint32_t h = 0; h < 2; ++h) {
-        tmem_ld_32x32b_x32(taddr + 32u * h, r);
+    for (uint32_t h = 0; h < 5; ++h) {
+        tmem_ld_32x32b_x16(taddr + 16u * h, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-        tmem_st_32x32b_x32(taddr + 32u * h, r);
+        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+        tmem_st_32x32b_x16(taddr + 16u * h, r);
     }
-    tmem_ld_32x32b_x16(taddr + 64u, r2);
-    tmem_ld_wait();
-#pragma unroll
-    for (int i = 0; i < 16; ++i) r2[i] = __float_as_uint(__uint_as_float(r2[i]) * f);
-    tmem_st_32x32b_x16(taddr + 64u, r2);
     tmem_st_wait();
 }
 
@@ -469,12 +465,12 @@ __device__ __forceinline__ void tc_scale_o(uint32_t taddr, float f) {
 //     (k_empty), issue the cp.async of K tile j (k_full completes when they
 //     land); once P(j-3) V(j-3) has read V buffer j % 3 (v_empty), the same
 //     for V tile j (v_full).  It never waits for its own copies.
-//   MMA warp, per key tile j: wait for P(j) (p_full, four softmax warps)
-//     and V tile j; issue O (+)= P(j) V(j) (commits o_full, v_empty); once
-//     K tile j+2 has landed, issue S(j+2) into the same TMEM buffer right
-//     behind it (commits s_full, k_empty): the tensor core executes one
-//     thread's MMAs in issue order, so S(j+2) writes only after P(j) V(j)
-//     has read P(j), and the MMA warp never waits for a product.
+//   P V issuer, per key tile j: wait for P(j) (p_full, four softmax warps)
+//     and V tile j; issue O (+)= P(j) V(j) (commits o_done[j % 2], v_empty).
+//   score issuer, per key tile j: once P(j-2) V(j-2) is done (o_done) and K
+//     tile j has landed, issue S(j) into TMEM buffer j % 2 (commits s_full,
+//     k_empty).  Two issuing threads keep the tensor core fed faster than
+//     one: a single thread issues about one MMA per 64 cycles.
 //   softmax warps (thread = query row = TMEM lane), per key tile j:
 //     wait for S(j), read the row, mask, row max, probabilities
 //     p = exp2(s * scale_log2 - m) against a reference m that moves only
@@ -485,8 +481,13 @@ __device__ __forceinline__ void tc_scale_o(uint32_t taddr, float f) {
 // the score tiles stream through them while the tensor core runs behind; a
 // softmax warp can be one key tile ahead of the slowest one (tile j+2 needs
 // S(j+2), which waits for P(j) V(j)).
+// Barrier phases: every waiter on a per-buffer barrier has itself seen the
+// phase before the one it waits for (k-th wait of a waiter = k-th phase),
+// and the next phase needs an arrival that follows its own, so a parity
+// wait always names the intended phase.
 // Every wait is bounded; an expired wait records its code, raises the CTA's
 // abort flag (every other wait then gives up too), and the roles unwind.
+// Two CTAs per SM (14 warps, 117 registers per thread).
 __global__ void __launch_bounds__(kTcThreads, 2)
 attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __restrict__ k, int64_t ldk,
                     const __half* __restrict__ v, int64_t ldv, const AttnTile* __restrict__ tiles,
@@ -498,9 +499,9 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     const uint32_t sK = base + kTcK, sV = base + kTcV;
     // per-buffer barriers: bar + 8 * buffer
     const uint32_t bar_s = base + kTcBar, bar_p = bar_s + 16, bar_kf = bar_s + 32, bar_vf = bar_s + 56,
-                   bar_ke = bar_s + 80, bar_ve = bar_s + 104, bar_o = bar_s + 128, bar_last = bar_s + 136,
-                   bar_q = bar_s + 144, bar_fin = bar_s + 152;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + (base - raw) + kTcBar + 160);
+                   bar_ke = bar_s + 80, bar_ve = bar_s + 104, bar_o = bar_s + 128, bar_last = bar_s + 144,
+                   bar_q = bar_s + 152, bar_fin = bar_s + 160;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + (base - raw) + kTcBar + 168);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const AttnTile t = tiles[blockIdx.x];
@@ -524,9 +525,10 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
             mbar_init(bar_ve + 8 * b, 1);
         }
         mbar_init(bar_o, 1);
+        mbar_init(bar_o + 8, 1);
         mbar_init(bar_last, 1);
         mbar_init(bar_q, 4);
-        mbar_init(bar_fin, 1);
+        mbar_init(bar_fin, 2);
         *abort_flag = 0u;
         fence_barrier_init();
     }
@@ -630,11 +632,12 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
             }
             if (j > 0 && __any_sync(0xffffffffu, move)) {
                 // O holds P(0..j-1) V against the old reference: wait for the
-                // last of those products.  S(j) was committed after P(j-2) V
-                // was issued, and a commit arrives only once every earlier
-                // MMA of its thread is done, so P(0..j-2) V are complete and
-                // this parity names P(j-1) V(j-1)
-                if (!tc_warp_wait(bar_o, (j - 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull)) break;
+                // last of those products.  S(j-1) and S(j) were issued after
+                // P(j-3) V and P(j-2) V completed, so o_done[(j-1) % 2] has
+                // passed P(j-3) V and this parity names P(j-1) V(j-1)
+                if (!tc_warp_wait(bar_o + 8u * ((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, timeout_ns, err,
+                                  kDevTimeoutTmemFull))
+                    break;
                 tc_fence_after();
                 tc_scale_o(tmem + lane_base + kTcColO, corr);
             }
@@ -698,25 +701,10 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
             }
         }
     } else if (warp == 4) {
-        // -------------------------------------------------------- MMA issue
+        // ------------------------------------------------------ P V issue
         const bool issuer = lane == 0 && !stall;
-        const uint32_t tq = tmem + kTcColQ;
-        bool ok = tc_warp_wait(bar_q, 0, abort_flag, timeout_ns, err, kDevTimeoutFull);
-        for (int j = 0; ok && j < 2 && j < n_kt; ++j) {
-            ok = tc_warp_wait(bar_kf + 8u * j, 0, abort_flag, timeout_ns, err, kDevTimeoutFull);
-            if (ok) {
-                fence_proxy_async_smem();
-                tc_fence_after();
-                if (issuer) {
-                    tc_issue_scores(tmem + 64u * j, tq, sK + kTcKBuf * j);
-                    mma_commit(bar_s + 8u * j);
-                    mma_commit(bar_ke + 8u * j);
-                }
-                __syncwarp();
-            }
-        }
         int b3 = 0, u3 = 0;   // j % 3 and j / 3
-        for (int j = 0; ok && j < n_kt; ++j) {
+        for (int j = 0; j < n_kt; ++j) {
             const uint32_t b = j & 1;
             if (!tc_warp_wait(bar_p + 8u * b, (j >> 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutEmpty)) break;
             if (!tc_warp_wait(bar_vf + 8u * b3, u3 & 1, abort_flag, timeout_ns, err, kDevTimeoutFull)) break;
@@ -724,34 +712,44 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
             tc_fence_after();
             if (issuer) {
                 tc_issue_pv(tmem + kTcColO, tmem + 64u * b, sV + kTcVBuf * b3, j > 0);
-                mma_commit(bar_o);
+                mma_commit(bar_o + 8u * b);
                 mma_commit(bar_ve + 8u * b3);
                 if (j + 1 == n_kt) mma_commit(bar_last);
             }
             __syncwarp();
-            if (j + 2 < n_kt) {
-                // S(j+2) overwrites P(j) in TMEM buffer b right behind the
-                // P(j) V(j) that reads it: the tensor core executes one
-                // thread's MMAs in issue order, so no wait is needed; K
-                // tile j+2 must have landed
-                const int b3n = b3 == 0 ? 2 : b3 - 1;               // (j + 2) % 3
-                const int u3n = b3 == 0 ? u3 : u3 + 1;              // (j + 2) / 3
-                if (!tc_warp_wait(bar_kf + 8u * b3n, u3n & 1, abort_flag, timeout_ns, err, kDevTimeoutFull)) break;
-                fence_proxy_async_smem();
-                tc_fence_after();
-                if (issuer) {
-                    tc_issue_scores(tmem + 64u * b, tq, sK + kTcKBuf * b3n);
-                    mma_commit(bar_s + 8u * b);
-                    mma_commit(bar_ke + 8u * b3n);
-                }
-                __syncwarp();
-            }
             if (++b3 == kTcStages) {
                 b3 = 0;
                 ++u3;
             }
         }
-    } else {
+    } else if (warp == 6) {
+        // --------------------------------------------------- score issue
+        const bool issuer = lane == 0 && !stall;
+        const uint32_t tq = tmem + kTcColQ;
+        bool ok = tc_warp_wait(bar_q, 0, abort_flag, timeout_ns, err, kDevTimeoutFull);
+        int b3 = 0, u3 = 0;   // j % 3 and j / 3
+        for (int j = 0; ok && j < n_kt; ++j) {
+            const uint32_t b = j & 1;
+            // S(j) overwrites P(j-2) in TMEM buffer b: P(j-2) V(j-2) must
+            // have read it
+            if (j >= 2 &&
+                !tc_warp_wait(bar_o + 8u * b, ((j - 2) >> 1) & 1, abort_flag, timeout_ns, err, kDevTimeoutTmemFull))
+                break;
+            if (!tc_warp_wait(bar_kf + 8u * b3, u3 & 1, abort_flag, timeout_ns, err, kDevTimeoutFull)) break;
+            fence_proxy_async_smem();
+            tc_fence_after();
+            if (issuer) {
+                tc_issue_scores(tmem + 64u * b, tq, sK + kTcKBuf * b3);
+                mma_commit(bar_s + 8u * b);
+                mma_commit(bar_ke + 8u * b3);
+            }
+            __syncwarp();
+            if (++b3 == kTcStages) {
+                b3 = 0;
+                ++u3;
+            }
+        }
+    } else if (warp == 5) {
         // ----------------------------------------------------------- loader
         // k_full / v_full [j % 3] phase j / 3 carries tile j; k_empty /
         // v_empty [j % 3] phase j / 3 is S(j) / P(j) V(j)
@@ -783,11 +781,13 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     tmem_st_wait();
     tc_fence_before();
     __syncthreads();
-    if (tid == 128) {   // the MMA issuer
+    if (tid == 128 || tid == 192) {   // the MMA issuers
         tc_fence_after();
         mma_commit(bar_fin);
-        volatile uint32_t no_abort = 0;
-        mbar_wait(bar_fin, 0, &no_abort, 100000000ull);
+        if (tid == 128) {
+            volatile uint32_t no_abort = 0;
+            mbar_wait(bar_fin, 0, &no_abort, 100000000ull);
+        }
     }
     __syncthreads();
     if (warp == 0) {
