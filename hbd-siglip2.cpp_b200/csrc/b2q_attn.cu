@@ -538,6 +538,12 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     }
     uint4 qv[9];
     if (warp < 4) {
+        // this thread's query row (zeros past the tile), into TMEM below;
+        // the loads are in flight during the constant stores
+        const bool ok = tid < t.q_rows;
+        const uint4* g = reinterpret_cast<const uint4*>(qh + (ok ? static_cast<int64_t>(tid) * ldq : 0));
+#pragma unroll
+        for (int c = 0; c < 9; ++c) qv[c] = ok ? __ldg(g + c) : make_uint4(0, 0, 0, 0);
         // constant parts: dims 72..79 (chunk 1 of atom 1) are zero in every
         // K buffer and hold 1.0 at dim 72 in every V buffer
         for (uint32_t i = tid; i < kTcStages * 64u; i += 128u) {
@@ -546,18 +552,9 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
             sts_v4(sV + b * kTcVBuf + 64u * 128u + sw128(r, 1), 0x00003C00u, 0, 0, 0);
         }
         fence_proxy_async_smem();
-        // this thread's query row (zeros past the tile), into TMEM below
-        const bool ok = tid < t.q_rows;
-        const uint4* g = reinterpret_cast<const uint4*>(qh + (ok ? static_cast<int64_t>(tid) * ldq : 0));
-#pragma unroll
-        for (int c = 0; c < 9; ++c) qv[c] = ok ? __ldg(g + c) : make_uint4(0, 0, 0, 0);
-    } else if (warp == 5) {
-        // key tiles 0 .. 2 (their arrivals follow the barrier below)
-        for (int j = 0; j < kTcStages && j < n_kt; ++j) {
-            const int k0 = j * kKT, valid = min(kKT, t.k_len - k0);
-            tc_load_tile(sK + kTcKBuf * j, kh + static_cast<int64_t>(k0) * ldk, ldk, valid, lane);
-            tc_load_tile(sV + kTcVBuf * j, vh + static_cast<int64_t>(k0) * ldv, ldv, valid, lane);
-        }
+    } else if (warp == 5 && n_kt > 0) {
+        // key tile 0 (its arrival follows the barrier below)
+        tc_load_tile(sK, kh, ldk, min(kKT, t.k_len), lane);
     }
     __syncthreads();
     tc_fence_after();
@@ -691,6 +688,7 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
                        __float_as_uint(__uint_as_float(r2[d + 3]) * inv));
             __syncwarp();
             const int rows = min(32, t.q_rows - warp * 32);
+#pragma unroll 4
             for (int r = 0; r < rows; ++r) {
                 const int rr = warp * 32 + r;
                 float* dst = out + static_cast<int64_t>(t.o_row0 + rr) * ldo + head * kDH;
@@ -752,10 +750,22 @@ attention_tc_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __r
     } else if (warp == 5) {
         // ----------------------------------------------------------- loader
         // k_full / v_full [j % 3] phase j / 3 carries tile j; k_empty /
-        // v_empty [j % 3] phase j / 3 is S(j) / P(j) V(j)
-        for (int j = 0; j < kTcStages && j < n_kt; ++j) {
-            cp_async_arrive_noinc(bar_kf + 8u * j);
-            cp_async_arrive_noinc(bar_vf + 8u * j);
+        // v_empty [j % 3] phase j / 3 is S(j) / P(j) V(j).
+        // Tiles 0..2 go in the order the MMAs take them: K0 K1 V0 K2 V1 V2.
+        // An arrival completes once every earlier copy of its lane has
+        // landed, so each one follows its own tile and no later tile.
+        for (int i = 0; i < 2 * kTcStages; ++i) {
+            const bool is_v = (0x34u >> i) & 1u;                        // K K V K V V
+            const int j = static_cast<int>((0x212010u >> (4 * i)) & 0xFu);   // 0 1 0 2 1 2
+            if (j >= n_kt) continue;
+            if (i > 0) {
+                const int k0 = j * kKT, valid = min(kKT, t.k_len - k0);
+                if (is_v)
+                    tc_load_tile(sV + kTcVBuf * j, vh + static_cast<int64_t>(k0) * ldv, ldv, valid, lane);
+                else
+                    tc_load_tile(sK + kTcKBuf * j, kh + static_cast<int64_t>(k0) * ldk, ldk, valid, lane);
+            }
+            cp_async_arrive_noinc((is_v ? bar_vf : bar_kf) + 8u * j);
         }
         int b3 = 0, u3 = 0;   // (j - 3) % 3 == j % 3 and (j - 3) / 3
         for (int j = kTcStages; j < n_kt; ++j) {
