@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark: Q8_0 SigLIP2-so400m vision tower, images/s.
+"""Benchmark: Q8_0 SigLIP2-so400m vision tower, images/s, on a 512-image NaFlex batch.
 
 One step = one batch of 512 NaFlex images (patch count uniform in [256, 1024]
 on a random grid, patches uniform in [-1, 1], PROBE pooling) through the full
@@ -188,9 +188,10 @@ def reference_arm(args):
     return 0
 
 
-def fc1_gemm(M, weights=None, reps=5):
+def fc1_gemm(M, weights=None, reps=5, gelu=True):
     """Time the fc1 Q8_0 GEMM (N=4304, K=1152) with the GELU->q8_1 epilogue
-    at M tokens; CUDA events on the launching stream.  -> (ms per launch, TOPS)"""
+    (or, gelu=False, the bias epilogue with fp32 output) at M tokens; CUDA
+    events on the launching stream.  -> (ms per launch, TOPS)"""
     import torch
     import b2q
     from b2q import synth
@@ -204,13 +205,21 @@ def fc1_gemm(M, weights=None, reps=5):
     b2q.quantize_q8_1(torch.randn((M, cfg.hidden), device="cuda"), act, M, cfg.hidden)
     bias = torch.zeros(cfg.ffn, device="cuda")
     stream = torch.cuda.current_stream()
+    y = None if gelu else torch.empty((M, cfg.ffn), dtype=torch.float32, device="cuda")
+
+    def launch():
+        if gelu:
+            b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
+        else:
+            b2q.mul_mat(W, act, M, y, kind=b2q.EPI_BIAS, bias=bias)
+
     for _ in range(3):
-        b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
+        launch()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(reps):
-        b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=bias, act_out=act_o)
+        launch()
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
@@ -218,12 +227,42 @@ def fc1_gemm(M, weights=None, reps=5):
     return ms, 2.0 * M * cfg.ffn * cfg.hidden / (ms * 1e-3) / 1e12
 
 
-def profile_gemm(tokens):
+def profile_gemm(tokens, epilogue="gelu"):
     import b2q
     b2q.init(0)
-    ms, tops = fc1_gemm(tokens, reps=2)
+    ms, tops = fc1_gemm(tokens, reps=2, gelu=epilogue == "gelu")
     b2q.check_device()
-    print(json.dumps({"kernel": "gemm_q8_kernel fc1", "tokens": tokens, "ms": ms, "tops": tops}), flush=True)
+    print(json.dumps({"kernel": "gemm_q8_kernel fc1", "epilogue": epilogue, "tokens": tokens, "ms": ms,
+                      "tops": tops}), flush=True)
+    return 0
+
+
+def profile_rowops(tokens):
+    """Time the two HBM-bound row kernels at `tokens` rows of 1152 (one CUDA
+    event pair over 5 launches each, after warm-up) and report GB/s on their
+    algorithmic bytes: LayerNorm->q8_1 reads 4*H and writes the q8_1 planes
+    (H value carriers + 4*H/32 scales); quantize reads 4*K and writes the same
+    planes.  The planes' value carriers are 1 byte (int8 operand mode) or 2
+    bytes (fp16 carriers, the default)."""
+    import torch
+    import b2q
+    b2q.init(0)
+    H = 1152
+    _, es, _, _ = b2q.act_layout(tokens, H)
+    x = torch.randn((tokens, H), device="cuda")
+    w = torch.ones(H, device="cuda")
+    b = torch.zeros(H, device="cuda")
+    act = b2q.act_empty(tokens, H)
+    plane_bytes = H * es + 4 * H // 32
+    _, hbm, src = peaks()
+    res = {"kernel": "rowops", "tokens": tokens, "carrier_bytes": es, "hbm_peak_gbs": hbm, "peak_source": src}
+    for name, fn in (("ln_quant_kernel", lambda: b2q.ln_quantize(x, w, b, 1e-6, tokens, H, act)),
+                     ("quantize_q8_1_kernel", lambda: b2q.quantize_q8_1(x, act, tokens, H))):
+        ms = min(_events_ms(fn, 5) for _ in range(3))
+        gbs = tokens * (4 * H + plane_bytes) / (ms * 1e-3) / 1e9
+        res[name] = {"ms": ms, "bytes_per_token": 4 * H + plane_bytes, "gbs": gbs, "frac_hbm": gbs / hbm}
+    b2q.check_device()
+    print(json.dumps(res), flush=True)
     return 0
 
 
@@ -274,8 +313,9 @@ def _events_ms(fn, reps, warm=2):
 
 
 def suite(args):
-    """BASELINE configs 1, 2, 3 and 5 on one GPU, one JSON line each (config 4
-    is the default bench line).  CPU counterparts: the CPU restatement (oracle/)
+    """The other workloads on one GPU, one JSON line each: batch-1 vision at 27x27
+    patches, the isolated GEMM sweep, the 5x64 text batch and zero-shot scoring
+    (the NaFlex batch is the default bench line).  CPU counterparts: the CPU restatement (oracle/)
     on all host threads, on the samples named in each line."""
     import math
     import torch
@@ -387,6 +427,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="TOKENS",
                     help="only run the fc1 GEMM (GELU->q8_1 epilogue) at this token count, for ncu captures")
+    ap.add_argument("--profile-epilogue", default="gelu", choices=["gelu", "f32"],
+                    help="--profile-gemm: GELU->q8_1 epilogue (default) or bias + fp32 output")
+    ap.add_argument("--profile-rowops", type=int, default=0, metavar="TOKENS",
+                    help="only time the LayerNorm->q8_1 and quantize kernels at this token count (GB/s)")
     ap.add_argument("--profile-attention", type=int, default=0, metavar="IMAGES",
                     help="only time one layer's attention over this many NaFlex images, both tensor-core kernels")
     ap.add_argument("--suite", action="store_true", help="configs 1, 2, 3 and 5 on one GPU (JSON lines)")
@@ -395,7 +439,9 @@ def main():
     if args.impl == "reference":
         return reference_arm(args)
     if args.profile_gemm:
-        return profile_gemm(args.profile_gemm)
+        return profile_gemm(args.profile_gemm, args.profile_epilogue)
+    if args.profile_rowops:
+        return profile_rowops(args.profile_rowops)
     if args.profile_attention:
         return profile_attention(args.profile_attention)
     if args.suite:

@@ -151,7 +151,7 @@ def init(device: int = 0, ops_mode: int = -1):
     check(lib().b2q_init(device, ops_mode))
 
 
-TUNE_GEMM_BN, TUNE_TIMEOUT_NS, TUNE_ATTN_EXACT, TUNE_TEST_STALL, TUNE_ATTN_KERNEL = 1, 2, 3, 4, 5
+TUNE_GEMM_BN, TUNE_TIMEOUT_NS, TUNE_ATTN_EXACT, TUNE_TEST_STALL, TUNE_ATTN_KERNEL, TUNE_GEMM_CTAS = 1, 2, 3, 4, 5, 6
 
 
 def tune(key: int, value: int):

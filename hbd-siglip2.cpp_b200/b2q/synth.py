@@ -76,7 +76,7 @@ def normal(name: str, shape, std: float, base_seed: int) -> np.ndarray:
 
 @dataclass
 class TowerConfig:
-    """SigLIP2-so400m geometry (BASELINE configs 1 and 3)."""
+    """SigLIP2-so400m geometry: width 1152, 27 layers, 16 heads, MLP 4304, 16x16 position table, vocab 256000."""
     hidden: int = 1152
     ffn: int = 4304
     n_head: int = 16
@@ -180,13 +180,13 @@ def text_checkpoint(cfg: TowerConfig | None = None, seed: int = 0, std: float = 
 
 
 def patches(n_tokens: int, patch_dim: int = 768, seed: int = 0) -> np.ndarray:
-    """Pixel patch vectors uniform in [-1, 1]."""
+    """Pixel patch vectors (16x16x3 = 768 values each) uniform in [-1, 1]."""
     rng = np.random.default_rng(0xB01D ^ seed)
     return rng.uniform(-1.0, 1.0, size=(n_tokens, patch_dim)).astype(np.float32)
 
 
 def naflex_grids(n_images: int, lo: int = 256, hi: int = 1024, seed: int = 0):
-    """Per-image (h, w) patch grids for BASELINE config 4: a patch budget drawn
+    """Per-image (h, w) patch grids for the NaFlex batch workload: a patch budget drawn
     uniformly from [lo, hi] and an aspect ratio log-uniform in [1/4, 4] (the
     range NaFlex resizing produces for ordinary photos), h = round(sqrt(n r)),
     w = floor(n / h), so h * w stays inside [lo - h, hi]."""
@@ -202,8 +202,8 @@ def naflex_grids(n_images: int, lo: int = 256, hi: int = 1024, seed: int = 0):
 
 
 def token_ids(n_prompts: int, n_pos: int = 64, vocab: int = 256000, seed: int = 0) -> np.ndarray:
-    """Token ids uniform in [1, vocab) with EOS id 1 at the last position
-    (BASELINE config 3)."""
+    """Token ids uniform in [1, vocab) with EOS id 1 at the last position, as
+    the text workloads use them (no padding mask)."""
     rng = np.random.default_rng(0x7E47 ^ seed)
     ids = rng.integers(1, vocab, size=(n_prompts, n_pos)).astype(np.int32)
     ids[:, -1] = 1

@@ -124,6 +124,10 @@ b2q_status b2q_tune(int key, int64_t value) {
             if (value != 0 && value != 1) return set_error(B2Q_ERR_INVALID, "attention kernel must be 0 or 1");
             ds->attn_kernel = static_cast<int>(value);
             return B2Q_OK;
+        case B2Q_TUNE_GEMM_CTAS:
+            if (value != 0 && value != 1 && value != 2) return set_error(B2Q_ERR_INVALID, "GEMM CTAs per SM must be 0, 1 or 2");
+            ds->gemm_ctas = static_cast<int>(value);
+            return B2Q_OK;
         default:
             return set_error(B2Q_ERR_INVALID, "unknown tuning key");
     }

@@ -30,10 +30,11 @@
 
 namespace b2q {
 
-template <int kOps, int kBN>
+template <int kOps, int kBN, int kCtas>
 struct GemmCfg {
     static constexpr int BM = 128;
     static constexpr int BN = kBN;
+    static constexpr int CTAS = kCtas;                     // resident CTAs per SM (1 or 2)
     static constexpr int ES = kOps == kOpsF16 ? 2 : 1;
     static constexpr int KROW = 128;                       // bytes of K per smem row per stage
     static constexpr int KBS = KROW / (32 * ES);           // K blocks per stage: 4 (i8) or 2 (f16)
@@ -42,22 +43,31 @@ struct GemmCfg {
     static constexpr int DX_BYTES = KBS * BM * 4;
     static constexpr int DW_BYTES = KBS * BN * 4;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + DX_BYTES + DW_BYTES;
-    static constexpr int STAGES = 4;                       // power of two: ring position is a mask
+    static constexpr int STAGES = kCtas == 1 ? 4 : 3;      // two CTAs share the SM's 228 KB
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-    static constexpr int EPI_WARPS = 8;
-    static constexpr int THREADS = 128 + EPI_WARPS * 32;   // 384: launch allocation 168 regs/thread
-    static constexpr int WG0_REGS = 40;                    // 128*40 + 256*232 = 384*168
+    // One CTA per SM: eight epilogue warps, two per TMEM lane quadrant, each
+    // owning half of the tile's columns.  Two CTAs per SM: four epilogue warps
+    // per CTA, one per quadrant, each owning all of its 32 rows' columns; the
+    // SM's two CTAs interleave, so one CTA's tile-end epilogue overlaps the
+    // other's K-block loop.
+    static constexpr int EPI_WARPS = kCtas == 1 ? 8 : 4;
+    static constexpr int THREADS = 128 + EPI_WARPS * 32;   // 384 or 256
+    static constexpr int LAUNCH_REGS = kCtas == 1 ? 168 : 128;
+    static constexpr int WG0_REGS = kCtas == 1 ? 40 : 24;  // producer / MMA warpgroup after setmaxnreg
     static constexpr int EPI_REGS = 232;
-    static constexpr int COLS = BN / 2;                    // columns per epilogue thread
+    static constexpr int COLS = BN * 4 / EPI_WARPS;        // columns per epilogue thread
     static constexpr int CC = COLS / 64;                   // 64-column chunks per epilogue thread
     static constexpr int CH = 2 * CC;                      // 16x256b.x8 TMEM loads per K block (2 slabs)
-    static constexpr int NBUF = 512 / BN;                  // accumulator ring depth (power of two)
-    static constexpr int TMEM_COLS = 512;
+    static constexpr int TMEM_COLS = 512 / kCtas;
+    static constexpr int NBUF = TMEM_COLS / BN;            // accumulator ring depth
     static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment for the swizzle");
     static_assert(CH % 2 == 0, "register double-buffer parity must repeat every K block");
-    static_assert(SMEM <= 227 * 1024, "shared memory budget");
-    static_assert(WG0_REGS * 128 + EPI_REGS * EPI_WARPS * 32 <= THREADS * 168, "register split exceeds the launch");
+    static_assert(NBUF >= 2, "the accumulator ring needs two buffers");
+    static_assert(SMEM * kCtas <= 227 * 1024, "shared memory budget");
+    static_assert(LAUNCH_REGS * THREADS * kCtas <= 65536, "launch register budget");
+    static_assert(WG0_REGS * 128 + EPI_REGS * EPI_WARPS * 32 <= THREADS * LAUNCH_REGS,
+                  "register split exceeds the launch");
 };
 
 struct GemmParams {
@@ -136,10 +146,10 @@ struct Smem {
 __device__ __forceinline__ uint32_t bar_at(uint32_t arr, uint32_t i) { return arr + 8u * i; }
 
 // ---------------------------------------------------------------- producer
-template <int kOps, int kBN>
+template <int kOps, int kBN, int kCtas>
 __device__ bool run_producer(const Smem& sm, const CUtensorMap* tmA, const CUtensorMap* tmB, const CUtensorMap* tmDX,
                              const CUtensorMap* tmDW, const GemmParams& p, uint32_t& issued) {
-    using Cfg = GemmCfg<kOps, kBN>;
+    using Cfg = GemmCfg<kOps, kBN, kCtas>;
     const int num_tiles = p.m_tiles * p.n_tiles;
     const int nst = (p.Kb + Cfg::KBS - 1) / Cfg::KBS;
     if (p.stall) return true;   // nothing issued: the consumers' bounded waits run out
@@ -168,9 +178,9 @@ __device__ bool run_producer(const Smem& sm, const CUtensorMap* tmA, const CUten
 }
 
 // ---------------------------------------------------------------- MMA issuer
-template <int kOps, int kBN>
+template <int kOps, int kBN, int kCtas>
 __device__ bool run_mma(const Smem& sm, uint32_t tmem_base, const GemmParams& p, uint32_t& issued) {
-    using Cfg = GemmCfg<kOps, kBN>;
+    using Cfg = GemmCfg<kOps, kBN, kCtas>;
     const uint32_t idesc = kOps == kOpsF16 ? idesc_f16_f32(Cfg::BM, Cfg::BN) : idesc_i8_s32(Cfg::BM, Cfg::BN);
     const int num_tiles = p.m_tiles * p.n_tiles;
     const int nst = (p.Kb + Cfg::KBS - 1) / Cfg::KBS;
@@ -227,9 +237,9 @@ __device__ bool run_mma(const Smem& sm, uint32_t tmem_base, const GemmParams& p,
 
 constexpr int kResBatch = 4;   // column groups (of 8) per batch of residual loads in store_tile
 
-template <int kOps, int kBN>
+template <int kOps, int kBN, int kCtas>
 __device__ __forceinline__ void store_tile(const GemmParams& p, float2* acc, int mrow0, int nblk0, int q) {
-    using Cfg = GemmCfg<kOps, kBN>;
+    using Cfg = GemmCfg<kOps, kBN, kCtas>;
     if (p.epi == B2Q_EPI_BIAS_GELU_Q8) {
         // In phases over the whole tile, so that the independent element
         // chains overlap: bias + GELU in place for all 64 pairs, then each
@@ -391,9 +401,9 @@ __device__ __forceinline__ void store_tile(const GemmParams& p, float2* acc, int
     }
 }
 
-template <int kOps, int kBN, bool kDump>
+template <int kOps, int kBN, int kCtas, bool kDump>
 __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParams& p, int warp, int lane) {
-    using Cfg = GemmCfg<kOps, kBN>;
+    using Cfg = GemmCfg<kOps, kBN, kCtas>;
     const int ew = warp - 4;
     const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
     const int col0 = (ew >> 2) * Cfg::COLS;     // first column of this warp's half of the tile
@@ -514,17 +524,17 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
             if (lane == 0) mbar_arrive(bar_at(sm.empty, s));
             st_ring.next();
         }
-        if constexpr (!kDump) store_tile<kOps, kBN>(p, acc, mrow0, nblk0, q);
+        if constexpr (!kDump) store_tile<kOps, kBN, kCtas>(p, acc, mrow0, nblk0, q);
     }
     return true;
 }
 
-template <int kOps, int kBN, bool kDump>
-__global__ void __launch_bounds__(GemmCfg<kOps, kBN>::THREADS, 1)
+template <int kOps, int kBN, int kCtas, bool kDump>
+__global__ void __launch_bounds__(GemmCfg<kOps, kBN, kCtas>::THREADS, kCtas)
 gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmDX, const __grid_constant__ CUtensorMap tmDW,
                const GemmParams p) {
-    using Cfg = GemmCfg<kOps, kBN>;
+    using Cfg = GemmCfg<kOps, kBN, kCtas>;
     extern __shared__ uint8_t smem_raw[];
     Smem sm;
     // the 128-byte swizzle needs 1024-byte aligned stages
@@ -569,7 +579,7 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tma_prefetch_desc(&tmDX);
             tma_prefetch_desc(&tmDW);
             uint32_t issued = 0;
-            run_producer<kOps, kBN>(sm, &tmA, &tmB, &tmDX, &tmDW, p, issued);
+            run_producer<kOps, kBN, kCtas>(sm, &tmA, &tmB, &tmDX, &tmDW, p, issued);
             // drain: never leave a copy in flight into this CTA's shared memory
             const uint32_t n_drain = issued < Cfg::STAGES ? issued : Cfg::STAGES;
             for (uint32_t i = 0; i < n_drain; ++i) {
@@ -579,7 +589,7 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
         } else if (warp == 1 && lane == 0) {
             uint32_t issued = 0;
-            run_mma<kOps, kBN>(sm, tmem_base, p, issued);
+            run_mma<kOps, kBN, kCtas>(sm, tmem_base, p, issued);
             // every issued MMA must have retired before TMEM is released
             if (issued > 0) {
                 volatile uint32_t no_abort = 0;
@@ -589,7 +599,7 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else {
         warpgroup_reg_alloc<Cfg::EPI_REGS>();
-        run_epilogue<kOps, kBN, kDump>(sm, tmem_base, p, warp, lane);
+        run_epilogue<kOps, kBN, kCtas, kDump>(sm, tmem_base, p, warp, lane);
         // an epilogue that gave up on an expired wait may still have a TMEM
         // load in flight: let it land before TMEM is released
         tmem_ld_wait();
@@ -605,21 +615,22 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
 // ------------------------------------------------------------------ host side
 
-template <int kOps, int kBN, bool kDump>
+template <int kOps, int kBN, int kCtas, bool kDump>
 static cudaError_t configure_once() {
     static bool done = false;
     if (done) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel<kOps, kBN, kDump>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GemmCfg<kOps, kBN>::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel<kOps, kBN, kCtas, kDump>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GemmCfg<kOps, kBN, kCtas>::SMEM);
     if (e == cudaSuccess) done = true;
     return e;
 }
 
 // Output columns [n_base, n_base + n_cols) of the GEMM, in kBN-column tiles
 // (n_base a multiple of kBN).
-template <int kOps, int kBN, bool kDump>
+template <int kOps, int kBN, int kCtas, bool kDump>
 static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s, int64_t n_base, int64_t n_cols) {
-    using Cfg = GemmCfg<kOps, kBN>;
+    using Cfg = GemmCfg<kOps, kBN, kCtas>;
     DeviceState* ds = state();
     const b2q_weight* w = a.w;
     const ActLayout L = act_layout(a.M, w->K, kOps);
@@ -656,11 +667,12 @@ static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s, int64_t n_base, in
         p.Kp_out = O.Kp;
         p.d_ld = O.ld;
     }
-    cudaError_t e = configure_once<kOps, kBN, kDump>();
+    cudaError_t e = configure_once<kOps, kBN, kCtas, kDump>();
     if (e != cudaSuccess) return cuda_check(e, "cudaFuncSetAttribute(gemm)");
     const int tiles = p.m_tiles * p.n_tiles;
-    const int grid = tiles < ds->num_sms ? tiles : ds->num_sms;
-    gemm_q8_kernel<kOps, kBN, kDump><<<grid, Cfg::THREADS, Cfg::SMEM, s>>>(tmA, *tmB, tmDX, *tmDW, p);
+    const int slots = ds->num_sms * kCtas;
+    const int grid = tiles < slots ? tiles : slots;
+    gemm_q8_kernel<kOps, kBN, kCtas, kDump><<<grid, Cfg::THREADS, Cfg::SMEM, s>>>(tmA, *tmB, tmDX, *tmDW, p);
     count_launch();
     return cuda_check(cudaGetLastError(), "gemm launch");
 }
@@ -677,15 +689,16 @@ static int64_t split_remainder(int64_t N) {
 }
 
 template <int kOps>
-static b2q_status dispatch_bn(const GemmArgs& a, cudaStream_t s, int bn, bool split) {
+static b2q_status dispatch_bn(const GemmArgs& a, cudaStream_t s, int bn, int ctas, bool split) {
     const int64_t N = a.w->N;
-    if (a.dump) return run_gemm<kOps, 128, true>(a, s, 0, N);
-    if (bn != 256) return run_gemm<kOps, 128, false>(a, s, 0, N);
+    if (a.dump) return run_gemm<kOps, 128, 1, true>(a, s, 0, N);
+    if (ctas == 2) return run_gemm<kOps, 128, 2, false>(a, s, 0, N);
+    if (bn != 256) return run_gemm<kOps, 128, 1, false>(a, s, 0, N);
     const int64_t rem = split ? split_remainder(N) : 0;
-    if (rem == 0) return run_gemm<kOps, 256, false>(a, s, 0, N);
-    b2q_status st = run_gemm<kOps, 256, false>(a, s, 0, N - rem);
+    if (rem == 0) return run_gemm<kOps, 256, 1, false>(a, s, 0, N);
+    b2q_status st = run_gemm<kOps, 256, 1, false>(a, s, 0, N - rem);
     if (st != B2Q_OK) return st;
-    return run_gemm<kOps, 128, false>(a, s, N - rem, rem);
+    return run_gemm<kOps, 128, 1, false>(a, s, N - rem, rem);
 }
 
 // Tile width when not forced by B2Q_TUNE_GEMM_BN: whichever of 256 and 128
@@ -704,11 +717,28 @@ static int auto_bn(int64_t M, int64_t N, int num_sms) {
     return 0.6 * static_cast<double>(r128) < 0.95 * r256 ? 128 : 256;
 }
 
+// Two CTAs per SM (128-column tiles, four epilogue warps each) when the
+// 128-column tiles give every SM at least one, except for the GELU -> q8_1
+// epilogue.  Measured at 65,536 and 313,755 tokens: QKV (fp16 out) +5%, O
+// projection and fc2 (bias + residual) +8%, fc1 with fp32 output +1-3%; the
+// GELU tile end, whose cost per thread is the same in both layouts, runs 3%
+// slower as two 128-column tiles.  At 54 tiles (729 tokens, N = 1152) the
+// eight-warp single CTA is faster.
+static int auto_ctas(int64_t M, int64_t N, int epi, int num_sms) {
+    if (epi == B2Q_EPI_BIAS_GELU_Q8) return 1;
+    const int64_t tiles128 = ((M + 127) / 128) * ((N + 127) / 128);
+    return tiles128 >= num_sms ? 2 : 1;
+}
+
 b2q_status launch_gemm(const GemmArgs& a, cudaStream_t s) {
     DeviceState* ds = state();
     const bool forced = ds->gemm_bn == 128 || ds->gemm_bn == 256;
     const int bn = forced ? ds->gemm_bn : auto_bn(a.M, a.w->N, ds->num_sms);
-    return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, bn, !forced) : dispatch_bn<kOpsI8>(a, s, bn, !forced);
+    const int ctas = ds->gemm_ctas == 1 || ds->gemm_ctas == 2
+                         ? ds->gemm_ctas
+                         : (forced ? 1 : auto_ctas(a.M, a.w->N, a.epi, ds->num_sms));
+    return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, bn, ctas, !forced)
+                                : dispatch_bn<kOpsI8>(a, s, bn, ctas, !forced);
 }
 
 // Weight tensor maps are built once at registration (box = 128 bytes of K by

@@ -36,6 +36,7 @@ struct DeviceState {
     uint32_t* err = nullptr;      // device error word (cudaMalloc'ed at init)
     uint64_t timeout_ns = 2000000000ull;
     int gemm_bn = 0;              // GEMM tile width: 128, 256, or 0 = by shape
+    int gemm_ctas = 0;            // GEMM CTAs per SM: 1, 2 (128-column tiles), or 0 = by shape
     int attn_exact = 0;           // attention in the checker's fixed fp32 order
     int attn_kernel = 0;          // 0 = tcgen05 kernel, 1 = mma.sync kernel
     int test_stall = 0;           // GEMM producer / attention MMA issuer idle (failure-path tests)

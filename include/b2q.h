@@ -69,13 +69,20 @@ b2q_status b2q_init(int device, int ops_mode);
  *                        faulting or hanging
  *   B2Q_TUNE_ATTN_KERNEL: tensor-core attention kernel: 0 = tcgen05 (TMEM
  *                        accumulators, 128 queries per CTA; default),
- *                        1 = mma.sync (64 queries per CTA) */
+ *                        1 = mma.sync (64 queries per CTA)
+ *   B2Q_TUNE_GEMM_CTAS:  GEMM CTAs resident per SM: 1 (eight epilogue warps
+ *                        per CTA), 2 (128-column tiles, four epilogue warps
+ *                        per CTA), 0 = chosen per shape and epilogue (2 when
+ *                        the 128-column tiles cover every SM, except for the
+ *                        GELU -> q8_1 epilogue).  Every setting gives
+ *                        bit-identical results. */
 enum {
     B2Q_TUNE_GEMM_BN = 1,
     B2Q_TUNE_TIMEOUT_NS = 2,
     B2Q_TUNE_ATTN_EXACT = 3,
     B2Q_TUNE_TEST_STALL = 4,
-    B2Q_TUNE_ATTN_KERNEL = 5
+    B2Q_TUNE_ATTN_KERNEL = 5,
+    B2Q_TUNE_GEMM_CTAS = 6
 };
 b2q_status b2q_tune(int key, int64_t value);
 /* Reads (and clears) the device error word after synchronising `stream`;

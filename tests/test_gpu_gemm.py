@@ -16,16 +16,21 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-@pytest.fixture(scope="module", params=[(b2q.OPS_F16, 0), (b2q.OPS_I8, 0), (b2q.OPS_F16, 128), (b2q.OPS_I8, 256)],
-                ids=["f16-auto", "i8-auto", "f16-bn128", "i8-bn256"])
+@pytest.fixture(scope="module", params=[(b2q.OPS_F16, 0, 0), (b2q.OPS_I8, 0, 0), (b2q.OPS_F16, 128, 1),
+                                        (b2q.OPS_I8, 256, 1), (b2q.OPS_F16, 0, 1), (b2q.OPS_F16, 0, 2),
+                                        (b2q.OPS_I8, 0, 2)],
+                ids=["f16-auto", "i8-auto", "f16-bn128", "i8-bn256", "f16-1cta", "f16-2cta", "i8-2cta"])
 def mode(request):
+    """(operand carriers, tile width, CTAs per SM); 0 = the library's choice."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    ops, bn = request.param
+    ops, bn, ctas = request.param
     b2q.init(0, ops)
     b2q.tune(b2q.TUNE_GEMM_BN, bn)
+    b2q.tune(b2q.TUNE_GEMM_CTAS, ctas)
     yield ops
     b2q.tune(b2q.TUNE_GEMM_BN, 0)
+    b2q.tune(b2q.TUNE_GEMM_CTAS, 0)
 
 
 def rand(shape, seed, scale=1.0):
@@ -180,8 +185,8 @@ def test_mul_mat_f32_ggml_semantics(oracle, mode):
 
 
 def test_full_size_sampled_rows(oracle, mode):
-    # BASELINE config-2 scale: M = 65536 rows; rows are independent, so the
-    # oracle checks a sample of them bit-exactly.
+    # The isolated-GEMM sweep's largest shape, M = 65536 rows; rows are
+    # independent, so the oracle checks a sample of them bit-exactly.
     M, N, K = 65536, 4304, 1152
     w_q = synth.quantize_q8_0(rand((N, K), 21, 0.02))
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -201,10 +206,12 @@ def test_full_size_sampled_rows(oracle, mode):
 
 @pytest.mark.parametrize("N,kind", [(1152, "residual"), (3456, "f16")])
 def test_large_m_column_split(oracle, mode, N, kind):
-    # At this M the automatic tile choice covers N = 1152 / 3456 with
-    # 256-column tiles up to the last multiple of 256 and a second launch of
-    # 128-column tiles for the remaining 128 columns; sampled rows are checked
-    # bit-exactly over every column, the seam at 1024 / 3328 included.
+    # At this M, with one CTA per SM (the f16-1cta / i8-bn256 modes), the
+    # tile choice covers N = 1152 / 3456 with 256-column tiles up to the last
+    # multiple of 256 and a second launch of 128-column tiles for the
+    # remaining 128 columns; the library's own choice (auto modes) runs two
+    # CTAs per SM on 128-column tiles.  Sampled rows are checked bit-exactly
+    # over every column, the seam at 1024 / 3328 included.
     M, K = 40000, 1152
     w_q = synth.quantize_q8_0(rand((N, K), 31, 0.02))
     bias = rand(N, 32, 0.1)

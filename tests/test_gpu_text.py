@@ -34,7 +34,7 @@ def exact_attention(dev):
 
 @pytest.fixture(scope="module")
 def config3(dev):
-    """27 layers, vocab 256000, 5 prompts x 64 ids."""
+    """Full text tower: 27 layers, vocab 256000, 5 prompts x 64 ids."""
     cfg = synth.TowerConfig()
     ck = synth.text_checkpoint(cfg, seed=7)
     ids = synth.token_ids(5, cfg.n_pos, cfg.vocab, seed=1)

@@ -7,7 +7,7 @@ Two bars:
   oracle's fixed fp32 operation order;
 * default tensor-core attention (fp16 Q, K, V as in the reference, the
   softmax probabilities carried as two fp16 halves, fp32 accumulation):
-  cosine >= 0.9999.  Any attention
+  cosine >= 0.9999 (the project's pooled-embedding bar).  Any attention
   that is not bit-reproducible moves some q8_1 rounding decisions downstream;
   over 27 layers that moves pooled values by up to ~0.03 (measured on the CPU
   between two oracle attention precisions: 0.023-0.028 on values of ~2), so
@@ -102,7 +102,7 @@ def test_tower_full_depth_one_image(oracle, dev):
 
 @pytest.mark.parametrize("kernel", [0, 1], ids=["tcgen05", "mma_sync"])
 def test_tower_naflex_batch_fast_vs_exact(dev, kernel):
-    # config-4 geometry at reduced batch: 24 NaFlex images of 256-1024 patches
+    # NaFlex batch geometry at reduced batch: 24 NaFlex images of 256-1024 patches
     # (the benchmark's grid generator), all 27 layers.  The exact attention
     # mode is bit-identical to the CPU restatement (tests above), so it serves
     # as the reference here; each tensor-core attention kernel must meet the
