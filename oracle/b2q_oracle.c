@@ -34,6 +34,28 @@ void orc_set_num_threads(int n) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* Element-rule variants (orc_set_rules).  The default (0) is the canonical  */
+/* order the CUDA kernels reproduce bit for bit.  The other bits switch the  */
+/* towers to the reference's own element rules, so that the distance        */
+/* between two faithful implementations of the same tower can be measured:  */
+/*   ORC_RULE_LN    LayerNorm as fused_layernorm_affine_kernel<1024>         */
+/*                  (src/cuda/siglip2_megakernel.cu:81-121): thread t of    */
+/*                  1024 sums elements t, t+1024, ...; xor butterflies      */
+/*                  16..1 inside each warp, then across the 32 warp sums;    */
+/*                  var = fma(-mean, mean, ss/H); inv = correctly rounded    */
+/*                  1/sqrt (the kernel's rsqrtf is approximate; its exact    */
+/*                  rounding is not reproducible on the CPU, and this        */
+/*                  stands in for it as another last-bit choice).            */
+/*   ORC_RULE_GELU  0.5*x*(1+tanhf(sqrt(2/pi)*x*(1+0.044715*x*x))) with the  */
+/*                  C library's tanhf (siglip2_megakernel.cu:276-280).       */
+/*   ORC_RULE_Q8    q8_1 with x*(127/a) rounded half away from zero.         */
+/*   ORC_RULE_GEMM  per-block accumulate acc += (dw*dx)*(float)S.            */
+/* ------------------------------------------------------------------------ */
+static int g_rules = 0;
+void orc_set_rules(int rules) { g_rules = rules; }
+int  orc_get_rules(void) { return g_rules; }
+
+/* ------------------------------------------------------------------------ */
 /* fp16 <-> fp32 (IEEE binary16, round-to-nearest-even)                      */
 /* ggml block_q8_0::d is an fp16 (ggml-common.h block_q8_0; gguf quants.py:389) */
 /* ------------------------------------------------------------------------ */
@@ -123,6 +145,17 @@ float orc_gelu(float x) {
 void orc_gelu_n(const float *x, int64_t n, float *y) {
     for (int64_t i = 0; i < n; ++i) y[i] = orc_gelu(x[i]);
 }
+
+/* The reference's own GELU expression with the C library's tanhf
+ * (ORC_RULE_GELU). */
+static float gelu_tanh_ref(float x) {
+    const float a = 0.044715f * x;
+    const float inner = fmaf(a, x, 1.0f);
+    const float y = (0.79788456080286535587989211986876f * x) * inner;
+    return (0.5f * x) * (1.0f + tanhf(y));
+}
+
+static inline float tower_gelu(float x) { return (g_rules & ORC_RULE_GELU) ? gelu_tanh_ref(x) : orc_gelu(x); }
 
 /* ------------------------------------------------------------------------ */
 /* Q8_0 weight codec — gguf-py quants.py:381-401 (bit-exact with            */
@@ -270,6 +303,7 @@ void orc_gemm_q8(const uint8_t *w, int64_t N, int64_t Kp,
             memcpy(wq + n * Kp + kb * 32, blk + 2, 32);
         }
     }
+    const int gemm_alt = (g_rules & ORC_RULE_GEMM) != 0;
     #pragma omp parallel for schedule(dynamic, 4)
     for (int64_t m = 0; m < M; ++m) {
         const int8_t *xr = qs + m * Kp;
@@ -281,8 +315,12 @@ void orc_gemm_q8(const uint8_t *w, int64_t N, int64_t Kp,
             for (int64_t kb = 0; kb < Kb; ++kb) {
                 int32_t S = dot32_i8(xr + kb * 32, wr + kb * 32);
                 if (block_sums) block_sums[(m * N + n) * Kb + kb] = S;
-                float t = (float) S * wdr[kb];
-                acc = fmaf(t, xd[kb], acc);
+                if (gemm_alt) {
+                    acc = fmaf(wdr[kb] * xd[kb], (float) S, acc);
+                } else {
+                    float t = (float) S * wdr[kb];
+                    acc = fmaf(t, xd[kb], acc);
+                }
             }
             y[m * N + n] = acc;
         }
@@ -330,8 +368,55 @@ static void row_moments(const float *x, int64_t H, float *mean_out, float *inv_u
     *mean_out = ps[0] / (float) H;
 }
 
+/* LayerNorm in the reference kernel's own order (ORC_RULE_LN, see above). */
+static void layernorm_ref_order(const float *xr, const float *w, const float *b, float eps, int64_t H, float *yr) {
+    float s[1024], ss[1024];
+    for (int t = 0; t < 1024; ++t) {
+        float a = 0.0f, q = 0.0f;
+        for (int64_t i = t; i < H; i += 1024) {
+            const float v = xr[i];
+            a = a + v;
+            q = fmaf(v, v, q);
+        }
+        s[t] = a;
+        ss[t] = q;
+    }
+    float ws[32], wss[32];
+    for (int wp = 0; wp < 32; ++wp) {
+        float ps[32], pss[32];
+        memcpy(ps, s + 32 * wp, sizeof ps);
+        memcpy(pss, ss + 32 * wp, sizeof pss);
+        for (int off = 16; off >= 1; off >>= 1) {
+            float ns[32], nss[32];
+            for (int l = 0; l < 32; ++l) { ns[l] = ps[l] + ps[l ^ off]; nss[l] = pss[l] + pss[l ^ off]; }
+            memcpy(ps, ns, sizeof ps);
+            memcpy(pss, nss, sizeof pss);
+        }
+        ws[wp] = ps[0];
+        wss[wp] = pss[0];
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+        float ns[32], nss[32];
+        for (int l = 0; l < 32; ++l) { ns[l] = ws[l] + ws[l ^ off]; nss[l] = wss[l] + wss[l ^ off]; }
+        memcpy(ws, ns, sizeof ws);
+        memcpy(wss, nss, sizeof wss);
+    }
+    const float mean = ws[0] / (float) H;
+    const float var = fmaf(-mean, mean, wss[0] / (float) H);
+    const float inv = (float) (1.0 / sqrt((double) (var + eps)));
+    for (int64_t i = 0; i < H; ++i) {
+        const float t = (xr[i] - mean) * inv;
+        yr[i] = t * w[i] + b[i];
+    }
+}
+
 void orc_layernorm(const float *x, const float *w, const float *b, float eps,
                    int64_t M, int64_t H, float *y) {
+    if (g_rules & ORC_RULE_LN) {
+        #pragma omp parallel for schedule(static)
+        for (int64_t m = 0; m < M; ++m) layernorm_ref_order(x + m * H, w, b, eps, H, y + m * H);
+        return;
+    }
     #pragma omp parallel for schedule(static)
     for (int64_t m = 0; m < M; ++m) {
         const float *xr = x + m * H;
@@ -508,7 +593,10 @@ static void proj(const uint8_t *w, int64_t N, int64_t K, int64_t Kp, const float
     if (quant_act) {
         int8_t *qs = (int8_t *) malloc((size_t) M * (size_t) Kp);
         float  *dx = (float *) malloc((size_t) M * (size_t) (Kp / 32) * sizeof(float));
-        orc_quantize_q8_1(x, M, K, K, Kp, qs, dx);
+        if (g_rules & ORC_RULE_Q8)
+            orc_quantize_q8_1_rule(x, M, K, K, Kp, qs, dx, 1);
+        else
+            orc_quantize_q8_1(x, M, K, K, Kp, qs, dx);
         orc_gemm_q8(w, N, Kp, qs, dx, M, y, NULL);
         free(qs);
         free(dx);
@@ -563,7 +651,7 @@ static void encoder_block(const orc_block *B, float *x, int64_t T, int64_t H, in
     proj(B->up_w, F, H, H, ln, T, quant_act, up);
     for (int64_t t = 0; t < T; ++t)
         for (int64_t i = 0; i < F; ++i)
-            up[t * F + i] = orc_gelu(up[t * F + i] + B->up_b[i]);
+            up[t * F + i] = tower_gelu(up[t * F + i] + B->up_b[i]);
     proj(B->down_w, H, F, Fp, up, T, quant_act, o);
     for (int64_t t = 0; t < T; ++t)
         for (int64_t i = 0; i < H; ++i)
@@ -658,7 +746,7 @@ int orc_vision_encode(const orc_vision_weights *W, const float *patches,
         add_bias(a, W->ho_b, 1, H);
         orc_layernorm(a, W->hln_w, W->hln_b, W->eps, 1, H, n1);
         proj(W->hup_w, W->F, H, H, n1, 1, quant_act, up);
-        for (int64_t i = 0; i < W->F; ++i) up[i] = orc_gelu(up[i] + W->hup_b[i]);
+        for (int64_t i = 0; i < W->F; ++i) up[i] = tower_gelu(up[i] + W->hup_b[i]);
         proj(W->hdown_w, H, W->F, W->Fp, up, 1, quant_act, dn);
         for (int64_t i = 0; i < H; ++i) out[i] = a[i] + (dn[i] + W->hdown_b[i]);
         free(q); free(qkv); free(k); free(v); free(att); free(a); free(n1); free(up); free(dn);

@@ -39,6 +39,17 @@
 extern "C" {
 #endif
 
+/* ---- element-rule variants (default 0: the canonical order above) ------- */
+/* The other rules are the reference's own element functions, used to
+ * measure how far two faithful implementations of a tower drift apart
+ * (b2q_oracle.c describes each). */
+#define ORC_RULE_LN   1
+#define ORC_RULE_GELU 2
+#define ORC_RULE_Q8   4
+#define ORC_RULE_GEMM 8
+void orc_set_rules(int rules);
+int  orc_get_rules(void);
+
 /* ---- scalar numerics ---------------------------------------------------- */
 float    orc_fp16_to_fp32(uint16_t h);
 uint16_t orc_fp32_to_fp16(float f);

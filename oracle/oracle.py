@@ -59,11 +59,28 @@ def _declare(L):
     L.orc_vision_encode.argtypes = [P, P, I64, I64, C.c_int, C.c_int, P]
     L.orc_text_encode.argtypes = [P, P, I64, C.c_int, P]
     L.orc_score.argtypes = [P, I64, P, I64, I64, C.c_float, C.c_float, P, P]
+    L.orc_set_rules.argtypes = [C.c_int]
+    L.orc_get_rules.restype = C.c_int
 
 
 def _p(a: np.ndarray):
     assert a.flags.c_contiguous
     return a.ctypes.data_as(C.c_void_p)
+
+
+RULE_LN, RULE_GELU, RULE_Q8, RULE_GEMM = 1, 2, 4, 8
+RULES_REFERENCE = RULE_LN | RULE_GELU | RULE_Q8 | RULE_GEMM
+
+
+def set_rules(rules: int):
+    """Switch the towers' element rules (0 = the canonical order the CUDA
+    kernels reproduce; RULES_REFERENCE = the reference kernels' own LayerNorm
+    order, tanhf GELU, half-away q8_1 and scale-product accumulation)."""
+    lib().orc_set_rules(int(rules))
+
+
+def get_rules() -> int:
+    return int(lib().orc_get_rules())
 
 
 def set_threads(n: int):

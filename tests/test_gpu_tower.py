@@ -7,12 +7,15 @@ Two bars:
   oracle's fixed fp32 operation order;
 * default tensor-core attention (fp16 Q, K, V as in the reference, the
   softmax probabilities carried as two fp16 halves, fp32 accumulation):
-  cosine >= 0.9999 (the project's pooled-embedding bar).  Any attention
-  that is not bit-reproducible moves some q8_1 rounding decisions downstream;
-  over 27 layers that moves pooled values by up to ~0.03 (measured on the CPU
-  between two oracle attention precisions: 0.023-0.028 on values of ~2), so
-  the max-abs bar here is 0.05 rather than the north star's 2e-3, which only
-  a bit-reproducible attention can meet (the exact mode does, with 0).
+  cosine >= 0.9999 (the project's pooled-embedding bar) and max-abs <= 0.05.
+  Any arithmetic that is not bit-identical moves some q8_1 rounding decisions
+  downstream, and over 27 layers that moves pooled values by ~0.025 (values
+  of ~2).  The CPU suite measures exactly this between the oracle and the
+  same tower evaluated with the reference kernels' own element rules (tanhf
+  GELU, the 1024-thread LayerNorm order, half-away q8_1;
+  test_oracle.py::test_reference_element_rules_drift): 0.024-0.028.  A
+  max-abs bar of 2e-3 can therefore only be met bit-identically (the exact
+  mode does, with 0), by the reference itself as much as by this library.
 """
 import numpy as np
 import pytest
@@ -74,11 +77,39 @@ def test_tower_bit_exact_small_batch(oracle, exact_attention, pooling):
 
 
 def test_tower_bit_exact_full_depth(oracle, exact_attention):
-    # all 27 layers at the reference's native 16x16 grid (config 1 geometry)
+    # all 27 layers at the position table's native 16x16 grid
     ck = synth.vision_checkpoint(synth.TowerConfig(), seed=0)
     grids = [(16, 16)]
     _, patches, got = run_tower(ck, grids, b2q.POOL_PROBE)
     assert_matches(oracle, ck, patches, grids, got, b2q.POOL_PROBE, exact=True)
+
+
+@pytest.fixture(scope="module")
+def grid27(oracle):
+    """The batch-1 workload: one 27x27-patch image through all 27 layers,
+    PROBE pooling, with its oracle embedding (computed once)."""
+    ck = synth.vision_checkpoint(synth.TowerConfig(), seed=0)
+    x = synth.patches(729, ck.cfg.patch_dim, seed=0)
+    return ck, x, oracle.vision_encode(ck, x, 27, 27, pooling=b2q.POOL_PROBE, quant_act=True)
+
+
+def test_tower_27x27_full_depth_bit_exact(grid27, exact_attention):
+    ck, x, ref = grid27
+    tower = b2q.VisionTower(ck.cfg)
+    tower.load(ck)
+    got = tower.encode(torch.from_numpy(x).cuda(), [(27, 27)], b2q.POOL_PROBE).cpu().numpy()
+    assert b2q.check_device() == 0
+    np.testing.assert_array_equal(got[0], ref)
+
+
+def test_tower_27x27_full_depth_tensor_core(grid27, dev):
+    ck, x, ref = grid27
+    tower = b2q.VisionTower(ck.cfg)
+    tower.load(ck)
+    got = tower.encode(torch.from_numpy(x).cuda(), [(27, 27)], b2q.POOL_PROBE).cpu().numpy()
+    assert b2q.check_device() == 0
+    c, e = cos(got[0], ref), float(np.abs(got[0] - ref).max())
+    assert c >= 0.9999 and e <= 0.05, (c, e)
 
 
 @pytest.mark.parametrize("pooling", [b2q.POOL_PROBE, b2q.POOL_MEAN])
@@ -93,7 +124,7 @@ def test_tower_small_batch_varlen(oracle, dev, pooling):
 
 
 def test_tower_full_depth_one_image(oracle, dev):
-    # all 27 layers, the reference's native 16x16 grid (config 1 geometry at 256 patches)
+    # all 27 layers at the position table's native 16x16 grid (256 patches)
     ck = synth.vision_checkpoint(synth.TowerConfig(), seed=0)
     grids = [(16, 16)]
     _, patches, got = run_tower(ck, grids, b2q.POOL_PROBE)
@@ -106,8 +137,7 @@ def test_tower_naflex_batch_fast_vs_exact(dev, kernel):
     # (the benchmark's grid generator), all 27 layers.  The exact attention
     # mode is bit-identical to the CPU restatement (tests above), so it serves
     # as the reference here; each tensor-core attention kernel must meet the
-    # tower bar against it on every image.  At this token count the projection
-    # GEMMs take 256-column tiles and the split 128-column remainder launches.
+    # tower bar against it on every image.
     ck = synth.vision_checkpoint(synth.TowerConfig(), seed=3)
     grids = synth.naflex_grids(24, seed=7)
     b2q.tune(b2q.TUNE_ATTN_KERNEL, kernel)
