@@ -417,13 +417,81 @@ def suite(args):
     return 0
 
 
+INT8_DATASHEET_TOPS = 4500.0
+INT8_DATASHEET_SOURCE = ("NVIDIA HGX B200 specifications: INT8 Tensor Core 72 POPS for 8 GPUs with sparsity, "
+                         "i.e. 4.5 POPS dense per GPU")
+
+
+def roofline_line(gemm_ms, gemm_tops, M, i8_peak):
+    """The fc1 GEMM against the int8 tensor-core roofline: the int8 dense
+    reference measured in this run (cuBLASLt int8 GEMM at 8192^3) when the
+    torch build has one, else the datasheet figure; both fractions and the
+    bf16 one are reported."""
+    bf16_peak, _, peak_src = peaks()
+    peak = i8_peak if i8_peak else INT8_DATASHEET_TOPS
+    traffic = (FC1_DRAM_BYTES_PER_TOKEN * M) if FC1_DRAM_BYTES_PER_TOKEN else None
+    return {"kernel": "gemm_q8_kernel (fc1, N=4304, K=1152, GELU->q8_1 epilogue)",
+            "bound": "tensor", "achieved": gemm_tops, "peak": peak, "unit": "TFLOP/s",
+            "op_kind": "int8 multiply-adds counted as 2 ops (TOPS)",
+            "frac": gemm_tops / peak,
+            "peak_source": ("int8 dense, measured in this run: cuBLASLt int8 x int8 -> int32 GEMM "
+                            "(torch._int_mm) at 8192^3, best of 10" if i8_peak else INT8_DATASHEET_SOURCE),
+            "int8_peak_measured": i8_peak,
+            "int8_peak_datasheet": INT8_DATASHEET_TOPS, "int8_datasheet_source": INT8_DATASHEET_SOURCE,
+            "frac_datasheet": gemm_tops / INT8_DATASHEET_TOPS,
+            "bf16_peak_measured": bf16_peak, "frac_bf16": gemm_tops / bf16_peak,
+            "bf16_peak_source": f"MEASURED_PEAKS.json bf16 burst ({peak_src})",
+            "launch_ms": gemm_ms, "M": M, "traffic": traffic}
+
+
+def timed(fn, steps, stream, world):
+    """Device time of `steps` calls of fn (CUDA events on `stream`, barrier
+    and synchronize on both sides) -> (max over ranks, this rank's) in ms."""
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    mine = e0.elapsed_time(e1)
+    ms = torch.tensor([mine], device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return float(ms.item()), mine
+
+
+def per_rank(values, world):
+    """All-gather a small list of floats from every rank -> list per rank."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    if world == 1:
+        return [values]
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="naflex", choices=["naflex", "zeroshot"],
+                    help="naflex: the 512-image NaFlex vision batch (default); zeroshot: 2048 images x 1000 "
+                         "prompts scored with both towers, images and prompts sharded over the ranks")
     ap.add_argument("--images", type=int, default=N_IMAGES)
+    ap.add_argument("--exact-attention", action="store_true",
+                    help="attention in the fixed fp32 order that makes the tower bit-identical to the CPU "
+                         "restatement (the parity-clean configuration)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="TOKENS",
                     help="only run the fc1 GEMM (GELU->q8_1 epilogue) at this token count, for ncu captures")
@@ -433,7 +501,8 @@ def main():
                     help="only time the LayerNorm->q8_1 and quantize kernels at this token count (GB/s)")
     ap.add_argument("--profile-attention", type=int, default=0, metavar="IMAGES",
                     help="only time one layer's attention over this many NaFlex images, both tensor-core kernels")
-    ap.add_argument("--suite", action="store_true", help="configs 1, 2, 3 and 5 on one GPU (JSON lines)")
+    ap.add_argument("--suite", action="store_true",
+                    help="the other workloads on one GPU (batch-1 vision, GEMM sweep, text, zero-shot), JSON lines")
     ap.add_argument("--out", default="", help="--suite: also write the JSON lines to this file")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -450,8 +519,6 @@ def main():
     import torch
     import torch.distributed as dist
     import b2q
-    from b2q import synth
-    from b2q.shard import gather_in_order, per_rank_capacity, shard_images
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -461,6 +528,25 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     b2q.init(local)
+    if args.exact_attention:
+        b2q.tune(b2q.TUNE_ATTN_EXACT, 1)
+    try:
+        if args.workload == "zeroshot":
+            run_zeroshot(args, world, rank)
+        else:
+            run_naflex(args, world, rank)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    return 0
+
+
+def run_naflex(args, world, rank):
+    import torch
+    import b2q
+    from b2q import synth
+    from b2q.shard import gather_in_order, per_rank_capacity, shard_images
 
     cfg = synth.TowerConfig()
     t0 = time.time()
@@ -482,20 +568,28 @@ def main():
         off += n
     dev = host.cuda()
     tower.reserve(my_tokens, len(my_grids))
-    per_rank = per_rank_capacity(args.images, world)
-    emb = torch.zeros((per_rank, cfg.hidden), dtype=torch.float32, device="cuda")
+    per_cap = per_rank_capacity(args.images, world)
+    emb = torch.zeros((per_cap, cfg.hidden), dtype=torch.float32, device="cuda")
     mine_dev = torch.tensor(mine, dtype=torch.int64, device="cuda")
     stream = torch.cuda.current_stream()
+    gather_events = []
 
-    def gather():
+    def gather(record=False):
         # pooled embeddings of all images, in the batch's order, on every rank
-        if world > 1:
-            return gather_in_order(emb[:len(mine)], mine_dev, args.images)
-        return emb[:len(mine)]
+        if world == 1:
+            return emb[:len(mine)]
+        if record:
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+        out = gather_in_order(emb[:len(mine)], mine_dev, args.images)
+        if record:
+            g1.record(stream)
+            gather_events.append((g0, g1))
+        return out
 
-    def step_device():
+    def step_device(record=False):
         tower.encode(dev, my_grids, b2q.POOL_PROBE, out=emb)
-        gather()
+        gather(record)
 
     out_host = np.empty((len(my_grids), cfg.hidden), np.float32)
     gathered_host = torch.empty((args.images, cfg.hidden), dtype=torch.float32, pin_memory=True)
@@ -513,23 +607,6 @@ def main():
             if rank == 0:
                 gathered_host.copy_(allemb)
 
-    def timed(fn, steps):
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        ms = torch.tensor([e0.elapsed_time(e1)], device="cuda")
-        if world > 1:
-            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        return float(ms.item())
-
     for _ in range(args.warmup):
         step_device()
     torch.cuda.synchronize()
@@ -538,23 +615,23 @@ def main():
     n0 = b2q.launch_count()
     gpus_used = list(range(args.gpus)) if rank == 0 else []
     with ClockSampler(gpus_used) as clk:
-        ms = timed(step_device, args.steps)
+        ms, my_ms = timed(lambda: step_device(True), args.steps, stream, world)
     launches = b2q.launch_count() - n0
     clocks = clk.summary()
     b2q.check_device()
+    gather_ms = (sum(a.elapsed_time(b) for a, b in gather_events) / len(gather_events)) if gather_events else 0.0
 
     # end to end through the host-buffer entry point
     step_e2e()
-    ms_e2e = timed(step_e2e, args.steps)
+    ms_e2e, _ = timed(step_e2e, args.steps, stream, world)
 
     # roofline of the dominant kernel: fc1 GEMM (N=4304, K=1152) with the
     # GELU->q8_1 epilogue at this rank's token count, CUDA events on the stream
     M = my_tokens
     gemm_ms, gemm_tops = fc1_gemm(M, weights=ck.tensors["v.blk.0.ffn_up.weight"])
-
     i8_peak = int8_peak_tops() if rank == 0 else None
+    ranks = per_rank([float(rank), float(my_tokens), float(len(mine)), my_ms / args.steps, gather_ms], world)
     if rank == 0:
-        bf16_peak, hbm_peak, peak_src = peaks()
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             O, ck_cpu, x, cores = cpu_tower_sample()
@@ -563,41 +640,142 @@ def main():
             dt = time.perf_counter() - t
             cpu = {"value": 1.0 / dt, "unit": "images/s", "cores": cores, "kind": "port",
                    "sample": f"1 image of {CPU_SIDE}x{CPU_SIDE} patches (the batch averages 613), PROBE pooling, "
-                             "CPU restatement (oracle/), "
+                             "CPU restatement (oracle/), AVX512-VNNI block dots where the host has them, "
                              "OpenMP over all host threads"}
         images = args.images * args.steps
-        traffic = (FC1_DRAM_BYTES_PER_TOKEN * M) if FC1_DRAM_BYTES_PER_TOKEN else None
         line = {
             "metric": METRIC, "value": images / (ms * 1e-3), "unit": "images/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": "config-4: 512 NaFlex images (256-1024 patches, random grids) through the "
+            "config": {"workload": "512 NaFlex images (256-1024 patches, random grids) through the "
                                    "27-layer Q8_0 SigLIP2-so400m vision tower, PROBE pooling",
                        "arithmetic": "Q8_0 x q8_1 int8 block dots, fp32 scales and accumulation",
+                       "attention": ("exact: fixed fp32 order, tower bit-identical to the CPU restatement"
+                                     if args.exact_attention else "tcgen05 tensor cores, fp16 Q/K/V"),
                        "global_batch": args.images, "tokens_per_step": total_tokens,
                        "parallelism": f"image-sharded replicas x{world} + NCCL all-gather",
                        "l2": "inputs and activations larger than L2 (no flush)"},
             "e2e": {"value": images / (ms_e2e * 1e-3), "unit": "images/s",
                     "h2d_bytes_per_step": int(total_tokens * PATCH_DIM * 4),
                     "d2h_bytes_per_step": int(args.images * cfg.hidden * 4)},
-            "roofline": {"kernel": "gemm_q8_kernel (fc1, N=4304, K=1152, GELU->q8_1 epilogue)",
-                         "bound": "tensor", "achieved": gemm_tops, "peak": bf16_peak / 1.0, "unit": "TFLOP/s",
-                         "frac": gemm_tops / bf16_peak, "peak_source": f"bf16 dense, {peak_src}",
-                         "launch_ms": gemm_ms, "M": M, "traffic": traffic,
-                         "int8_peak_measured": i8_peak,
-                         "frac_int8": (gemm_tops / i8_peak) if i8_peak else None},
+            "roofline": roofline_line(gemm_ms, gemm_tops, M, i8_peak),
             "gemm_tops": gemm_tops,
             "gpu_launches": int(launches),
             "clocks": clocks,
+            "ranks": [{"rank": int(r[0]), "tokens": int(r[1]), "images": int(r[2]), "ms_per_step": r[3],
+                       "gather_ms": r[4]} for r in ranks],
         }
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+
+
+def run_zeroshot(args, world, rank):
+    """Zero-shot scoring of 2048 images (27x27 patches, PROBE pooling) against
+    1000 prompts (64 random token ids, EOS last) with logit scale exp(log 10)
+    and bias -10: images and prompts split over the ranks, prompt embeddings
+    all-gathered, each rank scoring its images, score rows gathered in image
+    order (b2q.zeroshot).  One step is the whole job; value = images/s."""
+    import math
+    import torch
+    import b2q
+    from b2q import synth
+    from b2q.shard import shard_rows
+    from b2q.zeroshot import zero_shot
+
+    n_img, n_txt, side, chunk = 2048, 1000, 27, 512
+    ntok = side * side
+    cfg = synth.TowerConfig()
+    vt = b2q.VisionTower(cfg)
+    vt.load(synth.vision_checkpoint(cfg, seed=0))
+    tt = b2q.TextTower(cfg)
+    tt.load(synth.text_checkpoint(cfg, seed=0))
+    img_rows, txt_rows = shard_rows(n_img, rank, world), shard_rows(n_txt, rank, world)
+    n_mine = len(img_rows)
+    host = torch.empty((n_mine * ntok, PATCH_DIM), dtype=torch.float32, pin_memory=True)
+    for j, i in enumerate(img_rows):
+        host[j * ntok:(j + 1) * ntok] = torch.from_numpy(synth.patches(ntok, PATCH_DIM, seed=1000 + i))
+    ids_all = synth.token_ids(n_txt, cfg.n_pos, cfg.vocab, seed=2)
+    ids_host = torch.from_numpy(np.ascontiguousarray(ids_all[txt_rows.start:txt_rows.stop])).pin_memory()
+    dev_p = host.cuda()
+    ids_dev = ids_host.cuda()
+    vt.reserve(min(chunk, n_mine) * ntok, min(chunk, n_mine))
+    tt.reserve(max(1, len(txt_rows)))
+    img_emb = torch.empty((n_mine, cfg.hidden), device="cuda")
+    txt_emb = torch.empty((len(txt_rows), cfg.hidden), device="cuda")
+    probs_host = torch.empty((n_img, n_txt), dtype=torch.float32, pin_memory=True)
+    stream = torch.cuda.current_stream()
+
+    def enc_img(rows):
+        for c in range(0, n_mine, chunk):
+            k = min(chunk, n_mine - c)
+            vt.encode(dev_p[c * ntok:(c + k) * ntok], [(side, side)] * k, b2q.POOL_PROBE, out=img_emb[c:c + k])
+        return img_emb
+
+    def enc_txt(rows):
+        if len(rows):
+            tt.encode(ids_dev, out=txt_emb)
+        return txt_emb
+
+    def score(img, txt):
+        _, probs = b2q.score(img, txt, math.log(10.0), -10.0, logits=False)
+        return probs
+
+    events = {}
+
+    def step(record=False):
+        return zero_shot(enc_img, enc_txt, score, n_img, n_txt, rank, world, timings=events if record else None)
+
+    def step_e2e():
+        dev_p.copy_(host, non_blocking=True)
+        ids_dev.copy_(ids_host, non_blocking=True)
+        out = step()
+        if rank == 0:
+            probs_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    b2q.check_device()
+    n0 = b2q.launch_count()
+    with ClockSampler(list(range(args.gpus)) if rank == 0 else []) as clk:
+        ms, my_ms = timed(lambda: step(True), args.steps, stream, world)
+    launches = b2q.launch_count() - n0
+    clocks = clk.summary()
+    b2q.check_device()
+
+    def phase(a, b):
+        return sum(x.elapsed_time(y) for x, y in zip(events[a], events[b])) / len(events[a])
+
+    phases = [phase("start", "encoded"), phase("encoded", "text_gathered"), phase("text_gathered", "scored"),
+              phase("scored", "done")]
+    ms_e2e, _ = timed(step_e2e, args.steps, stream, world)
+    ranks = per_rank([float(rank), float(n_mine), float(len(txt_rows)), my_ms / args.steps] + phases, world)
+    if rank == 0:
+        line = {
+            "metric": "zero-shot images/s, 2048 images x 1000 prompts (both Q8_0 towers + sigmoid scoring)",
+            "value": n_img * args.steps / (ms * 1e-3), "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": "zero-shot: 2048 images of 27x27 patches (PROBE pooling) x 1000 prompts of 64 "
+                                   "token ids, L2-normalised, sigmoid(10 * dot - 10)",
+                       "parallelism": f"images and prompts sharded x{world}, prompt embeddings and score rows "
+                                      "all-gathered (NCCL)",
+                       "attention": ("exact" if args.exact_attention else "tcgen05 tensor cores (vision), "
+                                     "exact (text)"),
+                       "l2": "inputs and activations larger than L2 (no flush)"},
+            "e2e": {"value": n_img * args.steps / (ms_e2e * 1e-3), "unit": "images/s",
+                    "h2d_bytes_per_step": int(n_img * ntok * PATCH_DIM * 4 + n_txt * cfg.n_pos * 4),
+                    "d2h_bytes_per_step": int(n_img * n_txt * 4)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "ranks": [{"rank": int(r[0]), "images": int(r[1]), "prompts": int(r[2]), "ms_per_step": r[3],
+                       "encode_ms": r[4], "gather_text_ms": r[5], "score_ms": r[6], "gather_scores_ms": r[7]}
+                      for r in ranks],
+        }
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":
