@@ -10,6 +10,9 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#if defined(__x86_64__)
+#include <immintrin.h>
+#endif
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -286,9 +289,131 @@ static int32_t dot32_i8(const int8_t *a, const int8_t *b) {
     return s;
 }
 
+#if defined(__x86_64__)
+/* AVX512-VNNI form of the same GEMM, bit-identical to the scalar loop below:
+ * vpdpbusd multiplies unsigned by signed bytes, so the activation bytes are
+ * biased by +128 and the exact int32 correction 128*sum_j(w) is subtracted;
+ * then, per block, vcvtdq2ps (exact: |S| < 2^20), vmulps by the weight
+ * scales and vfmadd231ps with the activation scale, kb ascending: the same
+ * fp32 operations as (float)S*dw then fmaf(t, dx, acc).  Weights are packed
+ * per 16 output columns as [kb][j/4][16 columns][4 bytes], so one 64-byte
+ * load feeds 16 columns and the bias-corrected activation dword is
+ * broadcast; four rows share each weight load. */
+#define ORC_VNNI_TARGET __attribute__((target("avx512f,avx512bw,avx512vnni")))
+
+typedef struct {
+    int64_t N, Kb, NT;          /* NT = 16-column tiles */
+    int8_t *w;                  /* [NT][Kb][8][16][4] */
+    int32_t *wsum;              /* [NT][Kb][16] 128 * sum_j w */
+    float *wd;                  /* [NT][Kb][16] */
+} vnni_pack;
+
+static void vnni_pack_weights(const uint8_t *w, int64_t N, int64_t Kp, vnni_pack *P) {
+    const int64_t Kb = Kp / 32, NT = (N + 15) / 16;
+    P->N = N; P->Kb = Kb; P->NT = NT;
+    P->w = (int8_t *) calloc((size_t) (NT * Kb * 512), 1);
+    P->wsum = (int32_t *) calloc((size_t) (NT * Kb * 16), sizeof(int32_t));
+    P->wd = (float *) calloc((size_t) (NT * Kb * 16), sizeof(float));
+    #pragma omp parallel for schedule(static)
+    for (int64_t nt = 0; nt < NT; ++nt)
+        for (int64_t kb = 0; kb < Kb; ++kb)
+            for (int c = 0; c < 16; ++c) {
+                const int64_t n = nt * 16 + c;
+                if (n >= N) continue;
+                const uint8_t *blk = w + (n * Kb + kb) * 34;
+                uint16_t dh;
+                memcpy(&dh, blk, 2);
+                P->wd[(nt * Kb + kb) * 16 + c] = orc_fp16_to_fp32(dh);
+                int32_t sum = 0;
+                for (int j = 0; j < 32; ++j) {
+                    const int8_t v = (int8_t) blk[2 + j];
+                    P->w[(nt * Kb + kb) * 512 + (j / 4) * 64 + c * 4 + (j % 4)] = v;
+                    sum += v;
+                }
+                P->wsum[(nt * Kb + kb) * 16 + c] = 128 * sum;
+            }
+}
+
+ORC_VNNI_TARGET
+static void vnni_rows(const vnni_pack *P, const uint8_t *xu, const float *dx, int64_t Kp, int64_t m0, int R,
+                      int64_t nt, float *y, int64_t N) {
+    const int64_t Kb = P->Kb;
+    __m512 acc[4];
+    for (int r = 0; r < 4; ++r) acc[r] = _mm512_setzero_ps();
+    for (int64_t kb = 0; kb < Kb; ++kb) {
+        const int8_t *wb = P->w + (nt * Kb + kb) * 512;
+        __m512i S[4];
+        for (int r = 0; r < 4; ++r) S[r] = _mm512_setzero_si512();
+        for (int g = 0; g < 8; ++g) {
+            const __m512i wv = _mm512_loadu_si512((const void *) (wb + g * 64));
+            for (int r = 0; r < R; ++r) {
+                int32_t xd4;
+                memcpy(&xd4, xu + (m0 + r) * Kp + kb * 32 + g * 4, 4);
+                S[r] = _mm512_dpbusd_epi32(S[r], _mm512_set1_epi32(xd4), wv);
+            }
+        }
+        const __m512i corr = _mm512_loadu_si512((const void *) (P->wsum + (nt * Kb + kb) * 16));
+        const __m512 wd = _mm512_loadu_ps(P->wd + (nt * Kb + kb) * 16);
+        for (int r = 0; r < R; ++r) {
+            const __m512 t = _mm512_mul_ps(_mm512_cvtepi32_ps(_mm512_sub_epi32(S[r], corr)), wd);
+            acc[r] = _mm512_fmadd_ps(t, _mm512_set1_ps(dx[(m0 + r) * Kb + kb]), acc[r]);
+        }
+    }
+    const int64_t n0 = nt * 16;
+    const __mmask16 mask = (N - n0 >= 16) ? (__mmask16) 0xFFFF : (__mmask16) ((1u << (N - n0)) - 1u);
+    for (int r = 0; r < R; ++r) _mm512_mask_storeu_ps(y + (m0 + r) * N + n0, mask, acc[r]);
+}
+
+static int vnni_available(void) {
+    static int cached = -1;
+    if (cached < 0) {
+        __builtin_cpu_init();
+        cached = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+                 __builtin_cpu_supports("avx512vnni");
+        if (getenv("ORC_NO_VNNI")) cached = 0;
+    }
+    return cached;
+}
+
+static void gemm_q8_vnni(const uint8_t *w, int64_t N, int64_t Kp, const int8_t *qs, const float *dx, int64_t M,
+                         float *y) {
+    vnni_pack P;
+    vnni_pack_weights(w, N, Kp, &P);
+    uint8_t *xu = (uint8_t *) malloc((size_t) M * (size_t) Kp);
+    #pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < M * Kp; ++i) xu[i] = (uint8_t) ((int32_t) qs[i] + 128);
+    const int64_t MT = (M + 3) / 4;
+    #pragma omp parallel for schedule(dynamic, 1) collapse(2)
+    for (int64_t mt = 0; mt < MT; ++mt)
+        for (int64_t nt = 0; nt < P.NT; ++nt) {
+            const int64_t m0 = mt * 4;
+            const int R = (int) ((M - m0) < 4 ? (M - m0) : 4);
+            vnni_rows(&P, xu, dx, Kp, m0, R, nt, y, N);
+        }
+    free(xu);
+    free(P.w);
+    free(P.wsum);
+    free(P.wd);
+}
+#endif
+
+int orc_gemm_uses_vnni(void) {
+#if defined(__x86_64__)
+    return vnni_available();
+#else
+    return 0;
+#endif
+}
+
 void orc_gemm_q8(const uint8_t *w, int64_t N, int64_t Kp,
                  const int8_t *qs, const float *dx, int64_t M,
                  float *y, int32_t *block_sums) {
+#if defined(__x86_64__)
+    if (!block_sums && vnni_available() && (g_rules & ORC_RULE_GEMM) == 0) {
+        gemm_q8_vnni(w, N, Kp, qs, dx, M, y);
+        return;
+    }
+#endif
     const int64_t Kb = Kp / 32;
     /* unpack weights once: int8 plane + fp32 scales (exact fp16 widening) */
     int8_t *wq = (int8_t *) malloc((size_t) N * (size_t) Kp);
@@ -447,8 +572,90 @@ void orc_layernorm(const float *x, const float *w, const float *b, float eps,
  *   l = sum_k p_k (keys ascending) ; o_d = fma-chain over k of p_k*v_kd, / l
  * q/k/v point at head 0 of row 0 with row strides ldq/ldk/ldv; Lq query rows
  * attend to Lk keys; out rows stride ldo. */
+#if defined(__x86_64__)
+/* orc_expf on 16 lanes: the same operations in the same order (rint by
+ * vrndscaleps to nearest, the two-term reduction, the degree-8 polynomial,
+ * 2^n through the exponent field), so every lane equals orc_expf. */
+ORC_VNNI_TARGET
+static inline __m512 orc_expf_x16(__m512 x) {
+    const __m512 n = _mm512_roundscale_ps(_mm512_mul_ps(x, _mm512_set1_ps(ORC_LOG2E)),
+                                          _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC);
+    __m512 r = _mm512_fmadd_ps(n, _mm512_set1_ps(-ORC_LN2_HI), x);
+    r = _mm512_fmadd_ps(n, _mm512_set1_ps(-ORC_LN2_LO), r);
+    __m512 p = _mm512_set1_ps(2.48015873015873015873e-5f);
+    p = _mm512_fmadd_ps(p, r, _mm512_set1_ps(1.98412698412698412698e-4f));
+    p = _mm512_fmadd_ps(p, r, _mm512_set1_ps(1.38888888888888888889e-3f));
+    p = _mm512_fmadd_ps(p, r, _mm512_set1_ps(8.33333333333333333333e-3f));
+    p = _mm512_fmadd_ps(p, r, _mm512_set1_ps(4.16666666666666666667e-2f));
+    p = _mm512_fmadd_ps(p, r, _mm512_set1_ps(1.66666666666666666667e-1f));
+    p = _mm512_fmadd_ps(p, r, _mm512_set1_ps(0.5f));
+    p = _mm512_fmadd_ps(p, r, _mm512_set1_ps(1.0f));
+    p = _mm512_fmadd_ps(p, r, _mm512_set1_ps(1.0f));
+    const __m512i ni = _mm512_cvtps_epi32(n);
+    const __m512 sc = _mm512_castsi512_ps(_mm512_slli_epi32(_mm512_add_epi32(ni, _mm512_set1_epi32(127)), 23));
+    return _mm512_mul_ps(p, sc);
+}
+
+/* attention_q8 on 16 lanes, bit-identical to the scalar loop: scores with one
+ * key per lane (each lane's fma chain over d ascending, keys transposed to
+ * [d][key] per head), the row maximum and the key-ascending sum of p as in
+ * the scalar code, and the output with one dimension per lane (fma chain
+ * over keys ascending), divided by the sum. */
+ORC_VNNI_TARGET
+static void attention_q8_avx512(const float *q, int64_t ldq, const float *k, int64_t ldk, const float *v,
+                                int64_t ldv, int64_t Lq, int64_t Lk, int64_t n_head, int64_t dh, float *out,
+                                int64_t ldo) {
+    const float scale = 1.0f / sqrtf((float) dh);
+    const int64_t Lk16 = (Lk + 15) / 16 * 16;
+    const int64_t nd = (dh + 15) / 16;
+    for (int64_t hd = 0; hd < n_head; ++hd) {
+        float *kt = (float *) aligned_alloc(64, (size_t) (dh * Lk16) * sizeof(float));
+        float *vh = (float *) aligned_alloc(64, (size_t) (Lk * nd * 16) * sizeof(float));
+        for (int64_t d = 0; d < dh; ++d)
+            for (int64_t kk = 0; kk < Lk16; ++kk) kt[d * Lk16 + kk] = kk < Lk ? k[kk * ldk + hd * dh + d] : 0.0f;
+        for (int64_t kk = 0; kk < Lk; ++kk)
+            for (int64_t d = 0; d < nd * 16; ++d) vh[kk * nd * 16 + d] = d < dh ? v[kk * ldv + hd * dh + d] : 0.0f;
+        #pragma omp parallel for schedule(static)
+        for (int64_t qi = 0; qi < Lq; ++qi) {
+            const float *qr = q + qi * ldq + hd * dh;
+            float *sc = (float *) aligned_alloc(64, (size_t) Lk16 * sizeof(float));
+            for (int64_t k0 = 0; k0 < Lk16; k0 += 16) {
+                __m512 dot = _mm512_setzero_ps();
+                for (int64_t d = 0; d < dh; ++d)
+                    dot = _mm512_fmadd_ps(_mm512_set1_ps(qr[d]), _mm512_load_ps(kt + d * Lk16 + k0), dot);
+                _mm512_store_ps(sc + k0, _mm512_mul_ps(dot, _mm512_set1_ps(scale)));
+            }
+            float m = -INFINITY;
+            for (int64_t kk = 0; kk < Lk; ++kk) m = fmaxf(m, sc[kk]);
+            for (int64_t k0 = 0; k0 < Lk16; k0 += 16)
+                _mm512_store_ps(sc + k0, orc_expf_x16(_mm512_sub_ps(_mm512_load_ps(sc + k0), _mm512_set1_ps(m))));
+            float l = 0.0f;
+            for (int64_t kk = 0; kk < Lk; ++kk) l = l + sc[kk];
+            for (int64_t b = 0; b < nd; ++b) {
+                __m512 acc = _mm512_setzero_ps();
+                for (int64_t kk = 0; kk < Lk; ++kk)
+                    acc = _mm512_fmadd_ps(_mm512_set1_ps(sc[kk]), _mm512_loadu_ps(vh + kk * nd * 16 + b * 16), acc);
+                const __m512 o = _mm512_div_ps(acc, _mm512_set1_ps(l));
+                const int64_t rem = dh - b * 16;
+                const __mmask16 mk = rem >= 16 ? (__mmask16) 0xFFFF : (__mmask16) ((1u << rem) - 1u);
+                _mm512_mask_storeu_ps(out + qi * ldo + hd * dh + b * 16, mk, o);
+            }
+            free(sc);
+        }
+        free(kt);
+        free(vh);
+    }
+}
+#endif
+
 static void attention_q8(const float *q, int64_t ldq, const float *k, int64_t ldk, const float *v, int64_t ldv,
                          int64_t Lq, int64_t Lk, int64_t n_head, int64_t dh, float *out, int64_t ldo) {
+#if defined(__x86_64__)
+    if (vnni_available() && Lq > 1) {
+        attention_q8_avx512(q, ldq, k, ldk, v, ldv, Lq, Lk, n_head, dh, out, ldo);
+        return;
+    }
+#endif
     const float scale = 1.0f / sqrtf((float) dh);
     #pragma omp parallel for schedule(static) collapse(2)
     for (int64_t hd = 0; hd < n_head; ++hd) {
@@ -615,6 +822,7 @@ static void proj(const uint8_t *w, int64_t N, int64_t K, int64_t Kp, const float
 }
 
 static void add_bias(float *y, const float *b, int64_t M, int64_t N) {
+    #pragma omp parallel for schedule(static)
     for (int64_t m = 0; m < M; ++m)
         for (int64_t n = 0; n < N; ++n) y[m * N + n] = y[m * N + n] + b[n];
 }
@@ -633,6 +841,7 @@ static void encoder_block(const orc_block *B, float *x, int64_t T, int64_t H, in
     proj(B->qkv_w, 3 * H, H, H, ln, T, quant_act, qkv);
     add_bias(qkv, B->qkv_b, T, 3 * H);
     if (quant_act) {
+        #pragma omp parallel for schedule(static)
         for (int64_t i = 0; i < T * 3 * H; ++i) qkv[i] = half_of(qkv[i]);
         for (int64_t sidx = 0; sidx < n_seq; ++sidx) {
             const float *base = qkv + seq_off[sidx] * 3 * H;
@@ -643,16 +852,19 @@ static void encoder_block(const orc_block *B, float *x, int64_t T, int64_t H, in
         orc_attention(qkv, T, H, n_head, seq_off, seq_len, n_seq, att);
     }
     proj(B->o_w, H, H, H, att, T, quant_act, o);
+    #pragma omp parallel for schedule(static)
     for (int64_t t = 0; t < T; ++t)
         for (int64_t i = 0; i < H; ++i)
             x[t * H + i] = (o[t * H + i] + B->o_b[i]) + x[t * H + i];
 
     orc_layernorm(x, B->ln2_w, B->ln2_b, eps, T, H, ln);
     proj(B->up_w, F, H, H, ln, T, quant_act, up);
+    #pragma omp parallel for schedule(static)
     for (int64_t t = 0; t < T; ++t)
         for (int64_t i = 0; i < F; ++i)
             up[t * F + i] = tower_gelu(up[t * F + i] + B->up_b[i]);
     proj(B->down_w, H, F, Fp, up, T, quant_act, o);
+    #pragma omp parallel for schedule(static)
     for (int64_t t = 0; t < T; ++t)
         for (int64_t i = 0; i < H; ++i)
             x[t * H + i] = (o[t * H + i] + B->down_b[i]) + x[t * H + i];

@@ -81,6 +81,9 @@ void orc_quantize_q8_1_rule(const float *x, int64_t M, int64_t K, int64_t ldx, i
 void orc_gemm_q8(const uint8_t *w, int64_t N, int64_t Kp,
                  const int8_t *qs, const float *dx, int64_t M,
                  float *y, int32_t *block_sums);
+/* 1 when orc_gemm_q8 runs its AVX512-VNNI form on this host (bit-identical
+ * to the scalar loop; ORC_NO_VNNI in the environment forces the scalar one). */
+int orc_gemm_uses_vnni(void);
 
 /* ---- row ops ------------------------------------------------------------ */
 void orc_layernorm(const float *x, const float *w, const float *b, float eps,

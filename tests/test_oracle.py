@@ -297,3 +297,16 @@ def test_reference_element_rules_drift(oracle):
     c, e = cos(base, alt), float(np.abs(base - alt).max())
     assert c >= 0.9999, c
     assert e > 2e-3, e
+
+
+def test_vnni_gemm_is_the_scalar_gemm(oracle):
+    # orc_gemm_q8 runs an AVX512-VNNI form when the host has it; with
+    # block_sums requested it always runs the scalar loop, so the two results
+    # must be bit-identical (odd M and N exercise the row and column tails)
+    rng = np.random.default_rng(12)
+    for M, N, K in ((1, 16, 32), (7, 80, 1152), (33, 17, 64), (5, 1152, 4320)):
+        w = synth.quantize_q8_0((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        qs, dx = oracle.quantize_q8_1(rng.standard_normal((M, K)).astype(np.float32))
+        y_fast = oracle.gemm_q8(w, N, K, qs, dx)
+        y_scalar, _ = oracle.gemm_q8(w, N, K, qs, dx, block_sums=True)
+        np.testing.assert_array_equal(y_fast, y_scalar)
