@@ -25,6 +25,7 @@
 #include <unistd.h>
 
 #include <cmath>
+#include <cstdint>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -188,12 +189,21 @@ b2q_status bytes_of(const TensorInfo& t, size_t* out) {
         if (t.ne[d] <= 0 || n > INT64_MAX / t.ne[d]) return set_error(B2Q_ERR_SHAPE, "GGUF: bad shape of " + t.name);
         n *= t.ne[d];
     }
+    // element counts whose byte size would not fit a size_t are malformed
+    const uint64_t un = static_cast<uint64_t>(n);
     switch (t.type) {
-        case T_F32: *out = static_cast<size_t>(n) * 4; return B2Q_OK;
-        case T_F16: case T_BF16: *out = static_cast<size_t>(n) * 2; return B2Q_OK;
+        case T_F32:
+            if (un > SIZE_MAX / 4) return set_error(B2Q_ERR_SHAPE, "GGUF: tensor " + t.name + " too large");
+            *out = static_cast<size_t>(un) * 4;
+            return B2Q_OK;
+        case T_F16: case T_BF16:
+            if (un > SIZE_MAX / 2) return set_error(B2Q_ERR_SHAPE, "GGUF: tensor " + t.name + " too large");
+            *out = static_cast<size_t>(un) * 2;
+            return B2Q_OK;
         case T_Q8_0:
             if (t.ne[0] % 32) return set_error(B2Q_ERR_SHAPE, "GGUF: Q8_0 tensor " + t.name + " with ne0 % 32 != 0");
-            *out = static_cast<size_t>(n / 32) * 34;
+            if (un / 32 > SIZE_MAX / 34) return set_error(B2Q_ERR_SHAPE, "GGUF: tensor " + t.name + " too large");
+            *out = static_cast<size_t>(un / 32) * 34;
             return B2Q_OK;
         default:
             *out = 0;   // other types are listed but cannot be loaded into a tower
@@ -302,7 +312,9 @@ b2q_status b2q_gguf_open(const char* path, b2q_gguf** out) {
             delete g;
             return B2Q_ERR_SHAPE;
         }
-        if (t.offset > g->size || data_start + t.offset + t.nbytes > g->size)
+        // written so that no sum can wrap: data_start <= size, then the offset,
+        // then the byte count, each against what is left
+        if (data_start > g->size || t.offset > g->size - data_start || t.nbytes > g->size - data_start - t.offset)
             return fail("tensor " + t.name + " runs past the end of the file");
         t.data = static_cast<const uint8_t*>(m) + data_start + t.offset;
     }

@@ -21,12 +21,14 @@ namespace {
 // looked up below, never &g_noalloc_scratch.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[B2Q_NOALLOC_MAX_SCRATCH_BYTES];
 
+constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mutex;
-void* g_noalloc_addr[64] = {};   // per-device address of g_noalloc_scratch
+void* g_noalloc_addr[kMaxDevices] = {};   // per-device address of g_noalloc_scratch
 
 // Looks up (once per device, with that device current) the device address of
 // the scratch array.
 b2q_status noalloc_scratch(int device, void** out) {
+    if (device < 0 || device >= kMaxDevices) return b2q::set_error(B2Q_ERR_INVALID, "device index out of range");
     std::lock_guard<std::mutex> lk(g_noalloc_mutex);
     if (!g_noalloc_addr[device]) {
         void* p = nullptr;

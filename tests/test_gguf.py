@@ -87,3 +87,36 @@ def test_synthetic_checkpoint_lists_every_tensor(tmp_path):
     assert names["t.token_embd.weight"] == (b2q.GGML_Q8_0, (1152, 64))
     assert names["t.blk.0.ffn_down.weight"] == (b2q.GGML_Q8_0, (4320, 1152))
     assert names["t.final_ln.weight"] == (b2q.GGML_F32, (1152,))
+
+
+def _patched(data: bytes, name: str, ne0=None, offset=None) -> bytes:
+    """The file with one tensor-info entry's ne[0] and/or data offset
+    overwritten (entry layout: u64 name length, name, u32 n_dims,
+    u64 ne[n_dims], u32 type, u64 offset)."""
+    import struct
+    key = struct.pack("<Q", len(name)) + name.encode()
+    i = data.index(key) + len(key)
+    n_dims = struct.unpack_from("<I", data, i)[0]
+    b = bytearray(data)
+    if ne0 is not None:
+        struct.pack_into("<Q", b, i + 4, ne0)
+    if offset is not None:
+        struct.pack_into("<Q", b, i + 4 + 8 * n_dims + 4, offset)
+    return bytes(b)
+
+
+@pytest.mark.parametrize("field,value", [
+    ("ne0", 1 << 61),            # 2 x 2^61 F32 elements: 2^64 bytes, a size that wraps to 0
+    ("ne0", (1 << 61) - 1),      # 2^64 - 8 bytes: offset + size wraps past the file end
+    ("offset", (1 << 64) - 64),  # an offset that wraps when added to the data start
+    ("offset", 1 << 40),         # simply past the end of the file
+])
+def test_reader_rejects_overflowing_sizes(tmp_path, field, value):
+    # shapes or offsets whose byte arithmetic would wrap a 64-bit size are
+    # reported as errors, never accepted with a wrapped size
+    good = tmp_path / "good.gguf"
+    write(good, {"v.a": (np.ones((2, 8), np.float32), None)})
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(_patched(good.read_bytes(), "v.a", **{field: value}))
+    with pytest.raises(b2q.B2QError):
+        b2q.Gguf(bad)
