@@ -227,13 +227,14 @@ def fc1_gemm(M, weights=None, reps=5, gelu=True):
     return ms, 2.0 * M * cfg.ffn * cfg.hidden / (ms * 1e-3) / 1e12
 
 
-def profile_gemm(tokens, epilogue="gelu"):
+def profile_gemm(tokens, epilogue="gelu", ctas=0):
     import b2q
     b2q.init(0)
+    b2q.tune(b2q.TUNE_GEMM_CTAS, ctas)
     ms, tops = fc1_gemm(tokens, reps=2, gelu=epilogue == "gelu")
     b2q.check_device()
-    print(json.dumps({"kernel": "gemm_q8_kernel fc1", "epilogue": epilogue, "tokens": tokens, "ms": ms,
-                      "tops": tops}), flush=True)
+    print(json.dumps({"kernel": "gemm_q8_kernel fc1", "epilogue": epilogue, "ctas_per_sm": ctas or "auto",
+                      "tokens": tokens, "ms": ms, "tops": tops}), flush=True)
     return 0
 
 
@@ -497,6 +498,8 @@ def main():
                     help="only run the fc1 GEMM (GELU->q8_1 epilogue) at this token count, for ncu captures")
     ap.add_argument("--profile-epilogue", default="gelu", choices=["gelu", "f32"],
                     help="--profile-gemm: GELU->q8_1 epilogue (default) or bias + fp32 output")
+    ap.add_argument("--profile-ctas", type=int, default=0, choices=[0, 1, 2],
+                    help="--profile-gemm: GEMM CTAs per SM (0 = the library's choice)")
     ap.add_argument("--profile-rowops", type=int, default=0, metavar="TOKENS",
                     help="only time the LayerNorm->q8_1 and quantize kernels at this token count (GB/s)")
     ap.add_argument("--profile-attention", type=int, default=0, metavar="IMAGES",
@@ -508,7 +511,7 @@ def main():
     if args.impl == "reference":
         return reference_arm(args)
     if args.profile_gemm:
-        return profile_gemm(args.profile_gemm, args.profile_epilogue)
+        return profile_gemm(args.profile_gemm, args.profile_epilogue, args.profile_ctas)
     if args.profile_rowops:
         return profile_rowops(args.profile_rowops)
     if args.profile_attention:

@@ -61,6 +61,7 @@ namespace {
 struct Entry {
     b2q_weight* w;
     uint64_t generation;
+    int64_t N, K, row_bytes;
 };
 
 std::mutex g_mutex;
@@ -93,17 +94,18 @@ bool may_use_noalloc() {
 b2q_weight* weight_for(const ggml_tensor* w, cudaStream_t stream) {
     std::lock_guard<std::mutex> lk(g_mutex);
     const uint64_t gen = g_generation.load();
+    // ne0 = K (innermost), ne1 = N rows, nb1 = bytes per row of blocks
+    const int64_t N = w->ne[1], K = w->ne[0], row_bytes = static_cast<int64_t>(w->nb[1]);
     auto it = g_weights.find(w->data);
     if (it != g_weights.end()) {
-        if (it->second.generation == gen) return it->second.w;
-        b2q_weight_release(it->second.w);   // registered before an unload: stale
+        const Entry& e = it->second;
+        if (e.generation == gen && e.N == N && e.K == K && e.row_bytes == row_bytes) return e.w;
+        b2q_weight_release(e.w);   // registered before an unload, or another tensor now lives here
         g_weights.erase(it);
     }
     b2q_weight* h = nullptr;
-    // ne0 = K (innermost), ne1 = N rows, nb1 = bytes per row of blocks
-    if (b2q_weight_register(w->data, w->ne[1], w->ne[0], static_cast<int64_t>(w->nb[1]), 0, stream, &h) != B2Q_OK)
-        return nullptr;
-    g_weights.emplace(w->data, Entry{h, gen});
+    if (b2q_weight_register(w->data, N, K, row_bytes, 0, stream, &h) != B2Q_OK) return nullptr;
+    g_weights.emplace(w->data, Entry{h, gen, N, K, row_bytes});
     return h;
 }
 

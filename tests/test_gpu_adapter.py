@@ -36,6 +36,16 @@ def hook(tmp_path_factory):
     return L
 
 
+@pytest.fixture(autouse=True)
+def unload_between_tests(hook):
+    # each test is a model load: its weight buffers are freed afterwards and
+    # the allocator may hand their addresses to the next test, so the cached
+    # registrations are dropped the way the reference's unload path drops them
+    yield
+    torch.cuda.synchronize()
+    hook.b2q_ggml_release_weights()
+
+
 def tensor(ttype, ne, data, op=A.GGML_OP_NONE, src=()):
     t = A.GgmlTensor()
     t.type, t.op = ttype, op
