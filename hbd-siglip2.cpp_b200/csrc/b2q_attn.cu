@@ -272,20 +272,66 @@ attention_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __rest
 }
 
 // Exact mode: the fixed fp32 evaluation order of the CPU checker (one thread
-// per query row; fma chain over d for each score, scale, max; own exp;
-// sum of p over keys ascending; fma chain over keys for each output dim; one
-// division), so the whole tower can be verified bit for bit.  Scores are
-// recomputed in each of the three passes instead of rescaled online, which
-// would change the arithmetic.  A verification mode: ~3x the attention work.
+// per query row; fma chain over d for each score, scale, max; own exp; sum
+// of p over keys ascending; fma chain over keys for each output dim; one
+// division), so the whole tower can be verified bit for bit.  Two passes over
+// the keys: the first finds the row maximum, the second recomputes each
+// score, takes p = exp(s - max) and feeds both the running sum l and the 72
+// output chains (both ascending over keys, as in the checker; the sum is only
+// used at the end, so one pass serves both).  Scores are recomputed rather
+// than rescaled online, which would change the arithmetic.  Four keys' score
+// chains are evaluated side by side (each its own chain over d), so the
+// thread is not waiting on one FMA at a time.
 constexpr int kExactThreads = 64;
 constexpr int kExactKeys = 64;
+
+// Key rows are read four dimensions at a time (16-byte shared loads; a row
+// is 288 bytes, so every row starts 16-byte aligned), the products still
+// accumulated one dimension after the other.
+template <int kN>
+__device__ __forceinline__ void exact_scores(const float (&qv)[kDH], const float* sk, float scale, float (&sc)[kN]) {
+    float dot[kN];
+#pragma unroll
+    for (int j = 0; j < kN; ++j) dot[j] = 0.0f;
+#pragma unroll
+    for (int d4 = 0; d4 < kDH / 4; ++d4)
+#pragma unroll
+        for (int j = 0; j < kN; ++j) {
+            const float4 kv = *reinterpret_cast<const float4*>(sk + j * kDH + 4 * d4);
+            dot[j] = __fmaf_rn(qv[4 * d4 + 0], kv.x, dot[j]);
+            dot[j] = __fmaf_rn(qv[4 * d4 + 1], kv.y, dot[j]);
+            dot[j] = __fmaf_rn(qv[4 * d4 + 2], kv.z, dot[j]);
+            dot[j] = __fmaf_rn(qv[4 * d4 + 3], kv.w, dot[j]);
+        }
+#pragma unroll
+    for (int j = 0; j < kN; ++j) sc[j] = __fmul_rn(dot[j], scale);
+}
+
+__device__ __forceinline__ void store_halves8(float* dst, uint4 r) {
+    const __half2* h = reinterpret_cast<const __half2*>(&r);
+    const float2 a = __half22float2(h[0]), b = __half22float2(h[1]), c = __half22float2(h[2]),
+                 d = __half22float2(h[3]);
+    reinterpret_cast<float4*>(dst)[0] = make_float4(a.x, a.y, b.x, b.y);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(c.x, c.y, d.x, d.y);
+}
+
+__device__ __forceinline__ void exact_accumulate(float (&acc)[kDH], float pv, const float* sv) {
+#pragma unroll
+    for (int d4 = 0; d4 < kDH / 4; ++d4) {
+        const float4 vv = *reinterpret_cast<const float4*>(sv + 4 * d4);
+        acc[4 * d4 + 0] = __fmaf_rn(pv, vv.x, acc[4 * d4 + 0]);
+        acc[4 * d4 + 1] = __fmaf_rn(pv, vv.y, acc[4 * d4 + 1]);
+        acc[4 * d4 + 2] = __fmaf_rn(pv, vv.z, acc[4 * d4 + 2]);
+        acc[4 * d4 + 3] = __fmaf_rn(pv, vv.w, acc[4 * d4 + 3]);
+    }
+}
 
 __global__ void __launch_bounds__(kExactThreads)
 attention_exact_kernel(const __half* __restrict__ q, int64_t ldq, const __half* __restrict__ k, int64_t ldk,
                        const __half* __restrict__ v, int64_t ldv, const AttnTile* __restrict__ tiles,
                        float* __restrict__ out, int64_t ldo, float scale) {
-    __shared__ float sK[kExactKeys * kDH];
-    __shared__ float sV[kExactKeys * kDH];
+    __shared__ __align__(16) float sK[kExactKeys * kDH];
+    __shared__ __align__(16) float sV[kExactKeys * kDH];
     const AttnTile t = half_tile(tiles[blockIdx.x >> 1], blockIdx.x & 1);
     if (t.q_rows <= 0) return;
     const int head = blockIdx.y;
@@ -297,37 +343,62 @@ attention_exact_kernel(const __half* __restrict__ q, int64_t ldq, const __half* 
     for (int d = 0; d < kDH; ++d) qv[d] = __half2float(qrow[d]);
     const __half* kh = k + static_cast<int64_t>(t.k_row0) * ldk + head * kDH;
     const __half* vh = v + static_cast<int64_t>(t.k_row0) * ldv + head * kDH;
+    // key and value rows that start on 16-byte boundaries are read 8 halves at a time
+    const bool vec_rows = ((reinterpret_cast<uintptr_t>(kh) | reinterpret_cast<uintptr_t>(vh) |
+                            static_cast<uintptr_t>(ldk * 2) | static_cast<uintptr_t>(ldv * 2)) & 15u) == 0;
 
     float m = -INFINITY, l = 0.0f;
     float acc[kDH];
 #pragma unroll
     for (int d = 0; d < kDH; ++d) acc[d] = 0.0f;
 
-    for (int pass = 0; pass < 3; ++pass) {
+    for (int pass = 0; pass < 2; ++pass) {
         for (int k0 = 0; k0 < t.k_len; k0 += kExactKeys) {
             const int nk = min(kExactKeys, t.k_len - k0);
             __syncthreads();
-            for (int i = threadIdx.x; i < nk * kDH; i += kExactThreads) {
-                const int kk = i / kDH, d = i % kDH;
-                sK[i] = __half2float(kh[static_cast<int64_t>(k0 + kk) * ldk + d]);
-                if (pass == 2) sV[i] = __half2float(vh[static_cast<int64_t>(k0 + kk) * ldv + d]);
+            if (vec_rows) {
+                // 9 x 16-byte chunks of 8 halves per 72-dim row
+                for (int i = threadIdx.x; i < nk * 9; i += kExactThreads) {
+                    const int kk = i / 9, c = i - (i / 9) * 9;
+                    const uint4 kr = *reinterpret_cast<const uint4*>(kh + static_cast<int64_t>(k0 + kk) * ldk + 8 * c);
+                    store_halves8(sK + kk * kDH + 8 * c, kr);
+                    if (pass == 1) {
+                        const uint4 vr = *reinterpret_cast<const uint4*>(vh + static_cast<int64_t>(k0 + kk) * ldv + 8 * c);
+                        store_halves8(sV + kk * kDH + 8 * c, vr);
+                    }
+                }
+            } else {
+                for (int i = threadIdx.x; i < nk * kDH; i += kExactThreads) {
+                    const int kk = i / kDH, d = i % kDH;
+                    sK[i] = __half2float(kh[static_cast<int64_t>(k0 + kk) * ldk + d]);
+                    if (pass == 1) sV[i] = __half2float(vh[static_cast<int64_t>(k0 + kk) * ldv + d]);
+                }
             }
             __syncthreads();
-            for (int kk = 0; kk < nk; ++kk) {
-                float dot = 0.0f;
+            int kk = 0;
+            for (; kk + 4 <= nk; kk += 4) {
+                float sc[4];
+                exact_scores<4>(qv, sK + kk * kDH, scale, sc);
 #pragma unroll
-                for (int d = 0; d < kDH; ++d) dot = __fmaf_rn(qv[d], sK[kk * kDH + d], dot);
-                const float sc = __fmul_rn(dot, scale);
-                if (pass == 0) {
-                    m = fmaxf(m, sc);
-                } else {
-                    const float pv = own_expf(__fsub_rn(sc, m));
-                    if (pass == 1) {
-                        l = __fadd_rn(l, pv);
+                for (int j = 0; j < 4; ++j) {
+                    if (pass == 0) {
+                        m = fmaxf(m, sc[j]);
                     } else {
-#pragma unroll
-                        for (int d = 0; d < kDH; ++d) acc[d] = __fmaf_rn(pv, sV[kk * kDH + d], acc[d]);
+                        const float pv = own_expf(__fsub_rn(sc[j], m));
+                        l = __fadd_rn(l, pv);
+                        exact_accumulate(acc, pv, sV + (kk + j) * kDH);
                     }
+                }
+            }
+            for (; kk < nk; ++kk) {
+                float sc[1];
+                exact_scores<1>(qv, sK + kk * kDH, scale, sc);
+                if (pass == 0) {
+                    m = fmaxf(m, sc[0]);
+                } else {
+                    const float pv = own_expf(__fsub_rn(sc[0], m));
+                    l = __fadd_rn(l, pv);
+                    exact_accumulate(acc, pv, sV + kk * kDH);
                 }
             }
         }
