@@ -20,10 +20,12 @@
 // thread's 32-column TMEM load for the next chunk is in flight while it
 // computes the current one.
 //
-// Warp roles (384 threads, three warpgroups): warpgroup 0 holds the TMA
-// producer (warp 0) and the TMEM owner / MMA issuer (warp 1) and gives most of
-// its registers to warpgroups 1-2, the eight epilogue warps (two per 32-lane
-// TMEM quadrant, each owning BN/2 output columns of its 32 rows).
+// Warp roles: warpgroup 0 holds the TMA producer (warp 0) and the TMEM owner
+// / MMA issuer (warp 1) and gives most of its registers to the epilogue
+// warps.  Layouts (GemmCfg): one CTA per SM with eight epilogue warps (two
+// per 32-lane TMEM quadrant, each owning half of a 256- or 128-column tile's
+// columns), or two CTAs per SM with four epilogue warps each (one per
+// quadrant, all of a 128- or 64-column tile's columns).
 #include "b2q_internal.h"
 #include "b2q_numerics.cuh"
 #include "b2q_ptx.cuh"
@@ -42,9 +44,11 @@ struct GemmCfg {
     static constexpr int B_BYTES = BN * KROW;
     static constexpr int DX_BYTES = KBS * BM * 4;
     static constexpr int DW_BYTES = KBS * BN * 4;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + DX_BYTES + DW_BYTES;
-    static constexpr int STAGES = kCtas == 1 ? 4 : 3;      // two CTAs share the SM's 228 KB
+    static constexpr int LOAD_BYTES = A_BYTES + B_BYTES + DX_BYTES + DW_BYTES;   // TMA bytes per stage
+    static constexpr int STAGE_BYTES = (LOAD_BYTES + 1023) / 1024 * 1024;      // the swizzle needs 1024-byte stages
     static constexpr int BAR_BYTES = 256;
+    // two CTAs share the SM's 228 KB: four stages where they fit in half of it
+    static constexpr int STAGES = kCtas == 1 ? 4 : (4 * STAGE_BYTES + BAR_BYTES + 1024 <= 113 * 1024 ? 4 : 3);
     static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
     // One CTA per SM: eight epilogue warps, two per TMEM lane quadrant, each
     // owning half of the tile's columns.  Two CTAs per SM: four epilogue warps
@@ -164,7 +168,7 @@ __device__ bool run_producer(const Smem& sm, const CUtensorMap* tmA, const CUten
             }
             const uint32_t sbase = sm.base + s * Cfg::STAGE_BYTES;
             const uint32_t fb = bar_at(sm.full, s);
-            mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+            mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES);
             const int kx = st * (Cfg::KROW / Cfg::ES);
             tma_load_2d(sbase, tmA, fb, kx, mb * Cfg::BM);
             tma_load_2d(sbase + Cfg::A_BYTES, tmB, fb, kx, nb * Cfg::BN);
@@ -641,8 +645,8 @@ static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s, int64_t n_base, in
         !make_tmap_2d(&tmDX, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act + L.d_offset, L.M, L.Kb, L.ld * 4, Cfg::BM,
                       Cfg::KBS, false))
         return set_error(B2Q_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation planes");
-    const CUtensorMap* tmB = kBN == 256 ? &w->tm_q256 : &w->tm_q128;
-    const CUtensorMap* tmDW = kBN == 256 ? &w->tm_d256 : &w->tm_d128;
+    const CUtensorMap* tmB = kBN == 256 ? &w->tm_q256 : kBN == 128 ? &w->tm_q128 : &w->tm_q64;
+    const CUtensorMap* tmDW = kBN == 256 ? &w->tm_d256 : kBN == 128 ? &w->tm_d128 : &w->tm_d64;
 
     GemmParams p{};
     p.M = static_cast<int>(a.M);
@@ -692,6 +696,7 @@ template <int kOps>
 static b2q_status dispatch_bn(const GemmArgs& a, cudaStream_t s, int bn, int ctas, bool split) {
     const int64_t N = a.w->N;
     if (a.dump) return run_gemm<kOps, 128, 1, true>(a, s, 0, N);
+    if (bn == 64) return run_gemm<kOps, 64, 2, false>(a, s, 0, N);   // 64-column tiles exist in the two-CTA form
     if (ctas == 2) return run_gemm<kOps, 128, 2, false>(a, s, 0, N);
     if (bn != 256) return run_gemm<kOps, 128, 1, false>(a, s, 0, N);
     const int64_t rem = split ? split_remainder(N) : 0;
@@ -730,9 +735,19 @@ static int auto_ctas(int64_t M, int64_t N, int epi, int num_sms) {
     return tiles128 >= num_sms ? 2 : 1;
 }
 
+// Fewer 128-column tiles than SMs (small M): 64-column tiles, two CTAs per
+// SM, double the tiles.  Measured at M = 320-2,048: the N = 1152 projections
+// (O, fc2) gain 12-22% (fc2 at M = 729: 104 -> 126 TOPS), the wider ones are
+// within 2% of the best layout.
+static bool small_tiles(int64_t M, int64_t N, int num_sms) {
+    return ((M + 127) / 128) * ((N + 127) / 128) < num_sms;
+}
+
 b2q_status launch_gemm(const GemmArgs& a, cudaStream_t s) {
     DeviceState* ds = state();
-    const bool forced = ds->gemm_bn == 128 || ds->gemm_bn == 256;
+    const bool forced = ds->gemm_bn == 64 || ds->gemm_bn == 128 || ds->gemm_bn == 256;
+    if (!forced && ds->gemm_ctas == 0 && small_tiles(a.M, a.w->N, ds->num_sms))
+        return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, 64, 2, false) : dispatch_bn<kOpsI8>(a, s, 64, 2, false);
     const int bn = forced ? ds->gemm_bn : auto_bn(a.M, a.w->N, ds->num_sms);
     const int ctas = ds->gemm_ctas == 1 || ds->gemm_ctas == 2
                          ? ds->gemm_ctas
@@ -742,13 +757,15 @@ b2q_status launch_gemm(const GemmArgs& a, cudaStream_t s) {
 }
 
 // Weight tensor maps are built once at registration (box = 128 bytes of K by
-// BN rows, 128-byte swizzle; scales BN x blocks-per-stage), for both widths.
+// BN rows, 128-byte swizzle; scales BN x blocks-per-stage), for every width.
 bool make_weight_maps(b2q_weight* w) {
     const int es = ops_elem_bytes(w->mode);
     const uint32_t kbs = 128 / (32 * es);
     const CUtensorMapDataType dt = w->mode == kOpsF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
     return make_tmap_2d(&w->tm_q256, dt, w->q, w->K, w->N, w->K * es, 128 / es, 256, true) &&
            make_tmap_2d(&w->tm_q128, dt, w->q, w->K, w->N, w->K * es, 128 / es, 128, true) &&
+           make_tmap_2d(&w->tm_q64, dt, w->q, w->K, w->N, w->K * es, 128 / es, 64, true) &&
+           make_tmap_2d(&w->tm_d64, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 64, kbs, false) &&
            make_tmap_2d(&w->tm_d256, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 256, kbs, false) &&
            make_tmap_2d(&w->tm_d128, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 128, kbs, false);
 }
