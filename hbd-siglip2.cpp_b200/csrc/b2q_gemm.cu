@@ -312,11 +312,15 @@ __device__ __forceinline__ void store_tile(const GemmParams& p, float2* acc, int
                         for (int gg = 0; gg < 4; ++gg) {
                             const float2 v = acc[16 * (2 * cc + s) + 2 * (4 * bl + gg) + h];
                             const int64_t off = static_cast<int64_t>(m) * p.Kp_out + n0 + 8 * gg + 2 * q;
-                            const int32_t q0 = q8_round(v.x, inv), q1 = q8_round(v.y, inv);
                             if constexpr (kOps == kOpsF16) {
+                                // q = rint(x * inv) on the fp32 adder (q8_round_adder2); |x| <= a
+                                // bounds |x * inv| below 127.5, so q needs no clamp, and the
+                                // integer packs into its fp16 carrier exactly
+                                const float2 qf = q8_round_adder2(v, inv);
                                 reinterpret_cast<__half2*>(reinterpret_cast<__half*>(p.q_out) + off)[0] =
-                                    __halves2half2(__int2half_rn(q0), __int2half_rn(q1));
+                                    __floats2half2_rn(qf.x, qf.y);
                             } else {
+                                const int32_t q0 = q8_round(v.x, inv), q1 = q8_round(v.y, inv);
                                 const uint32_t lo = static_cast<uint32_t>(q0) & 0xFFu;
                                 const uint32_t hi = static_cast<uint32_t>(q1) & 0xFFu;
                                 reinterpret_cast<uint16_t*>(reinterpret_cast<int8_t*>(p.q_out) + off)[0] =

@@ -58,6 +58,14 @@ __device__ __forceinline__ float2 own_div2(float2 a, float2 b) {
 // difference of the bit patterns.  Identical to rintf / __float2int_rn on
 // that range, without the conversion pipe.
 constexpr float kRintMagic = 12582912.0f;   // 1.5 * 2^23, bits 0x4B400000
+
+// a * b per lane, each product rounded on its own.  The scalar __fmul_rn is
+// documented never to be merged into a multiply-add; a packed product that
+// feeds a packed add can be (measured: the rounding adders below then saw
+// the unrounded product and chose the other integer near .5 ties).
+__device__ __forceinline__ float2 fmul2_rounded(float2 a, float2 b) {
+    return make_float2(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y));
+}
 __device__ __forceinline__ float2 rint2_adder(float2 t, int32_t& n0, int32_t& n1) {
     const float2 tm = __fadd2_rn(t, make_float2(kRintMagic, kRintMagic));
     n0 = __float_as_int(tm.x) - 0x4B400000;
@@ -73,7 +81,7 @@ __device__ __forceinline__ float2 gelu2(float2 x) {
     z.x = fminf(fmaxf(z.x, -80.0f), 80.0f);
     z.y = fminf(fmaxf(z.y, -80.0f), 80.0f);
     // e^z, as own_expf
-    const float2 t = __fmul2_rn(z, make_float2(1.44269504088896340736f, 1.44269504088896340736f));
+    const float2 t = fmul2_rounded(z, make_float2(1.44269504088896340736f, 1.44269504088896340736f));
     int32_t n0, n1;   // |t| <= 80 * log2(e)
     const float2 n = rint2_adder(t, n0, n1);
     float2 r = __ffma2_rn(n, make_float2(-0.693145751953125f, -0.693145751953125f), z);
@@ -85,6 +93,8 @@ __device__ __forceinline__ float2 gelu2(float2 x) {
 #pragma unroll
     for (int i = 1; i < 9; ++i) p = __ffma2_rn(p, r, make_float2(kc[i], kc[i]));
     const float2 sc = make_float2(__int_as_float((n0 + 127) << 23), __int_as_float((n1 + 127) << 23));
+    // p * 2^n is exact (a normal number scaled by a power of two), so it does
+    // not matter whether the product and the add are fused
     const float2 d = __fadd2_rn(make_float2(1.0f, 1.0f), __fmul2_rn(p, sc));
     return own_div2(x, d);
 }
@@ -98,6 +108,18 @@ __device__ __forceinline__ float q8_scale(float amax) { return __fdiv_rn(amax, 1
 __device__ __forceinline__ int q8_round(float x, float inv) {
     int q = __float2int_rn(__fmul_rn(x, inv));
     return q > 127 ? 127 : (q < -128 ? -128 : q);
+}
+
+// The same rule for two values of one block whose absmax is a (inv = 127/a
+// rounded): |x| <= a bounds |x * inv| by 127 * (1 + 2^-24), below 127.5, so
+// the rounded value already lies in [-127, 127] and the clamp never applies.
+// Rounding to nearest even is done on the fp32 adder (t + 1.5 * 2^23 rounds
+// t to an integer for |t| < 2^22; subtracting the constant back is exact).
+// Returns the integers as floats, identical to q8_round's results.
+__device__ __forceinline__ float2 q8_round_adder2(float2 x, float inv) {
+    const float2 t = fmul2_rounded(x, make_float2(inv, inv));
+    const float2 tm = __fadd2_rn(t, make_float2(kRintMagic, kRintMagic));
+    return __fadd2_rn(tm, make_float2(-kRintMagic, -kRintMagic));
 }
 
 }  // namespace b2q

@@ -205,6 +205,35 @@ def test_full_size_sampled_rows(oracle, mode):
     np.testing.assert_array_equal(y[torch.from_numpy(rows).cuda()].cpu().numpy(), oracle.gemm_q8(w_q, N, K, qs, dx))
 
 
+def test_full_size_gelu_quantize_sampled_rows(oracle, mode):
+    # The fc1 tile end at full size (bias, GELU, q8_1 planes of 4304 -> 4320
+    # columns) against the oracle on 2,000 sampled rows: 8.6 M quantized
+    # values, enough to meet the rare products that round to a .5 tie, where
+    # a rounding step that is not taken exactly as the oracle takes it picks
+    # the other integer.
+    M, N, K = 65536, 4304, 1152
+    w_q = synth.quantize_q8_0(rand((N, K), 41, 0.02))
+    bias = rand(N, 42, 0.1)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randn((M, K), generator=g, device="cuda")
+    W = b2q.Weight(w_q, N, K)
+    act = b2q.act_empty(M, K)
+    b2q.quantize_q8_1(x, act, M, K)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    b2q.mul_mat(W, act, M, y, kind=b2q.EPI_BIAS, bias=dev(bias))
+    out = b2q.act_empty(M, N)
+    b2q.mul_mat(W, act, M, None, kind=b2q.EPI_BIAS_GELU_Q8, bias=dev(bias), act_out=out)
+    torch.cuda.synchronize()
+    assert b2q.check_device() == 0
+    rows = np.random.default_rng(3).integers(0, M, 2000)
+    idx = torch.from_numpy(rows).cuda()
+    q_ref, d_ref = oracle.quantize_q8_1(oracle.gelu_vec(y[idx].cpu().numpy()), 4320)
+    q, d = b2q.act_planes(out, M, N)
+    np.testing.assert_array_equal(q[idx].cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(d[idx].cpu().numpy(), d_ref)
+    W.release()
+
+
 @pytest.mark.parametrize("N,kind", [(1152, "residual"), (3456, "f16")])
 def test_large_m_column_split(oracle, mode, N, kind):
     # At this M, with one CTA per SM (the f16-1cta / i8-bn256 modes), the
