@@ -258,7 +258,7 @@ def profile_rowops(tokens):
     _, hbm, src = peaks()
     res = {"kernel": "rowops", "tokens": tokens, "carrier_bytes": es, "hbm_peak_gbs": hbm, "peak_source": src}
     for name, fn in (("ln_quant_kernel", lambda: b2q.ln_quantize(x, w, b, 1e-6, tokens, H, act)),
-                     ("quantize_q8_1_kernel", lambda: b2q.quantize_q8_1(x, act, tokens, H))):
+                     ("quantize_rows_kernel", lambda: b2q.quantize_q8_1(x, act, tokens, H))):
         ms = min(_events_ms(fn, 5) for _ in range(3))
         gbs = tokens * (4 * H + plane_bytes) / (ms * 1e-3) / 1e9
         res[name] = {"ms": ms, "bytes_per_token": 4 * H + plane_bytes, "gbs": gbs, "frac_hbm": gbs / hbm}
