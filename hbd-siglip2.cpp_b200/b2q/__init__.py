@@ -21,7 +21,7 @@ EPI_NONE, EPI_BIAS, EPI_BIAS_RESIDUAL, EPI_BIAS_GELU_Q8, EPI_BIAS_F16 = 0, 1, 2,
 
 #: every symbol include/b2q.h declares (checked by the CPU test suite)
 EXPORTS = [
-    "b2q_last_error", "b2q_abi_version", "b2q_launch_count", "b2q_init", "b2q_tune", "b2q_check_device",
+    "b2q_last_error", "b2q_abi_version", "b2q_launch_count", "b2q_graph_launch_count", "b2q_init", "b2q_tune", "b2q_check_device",
     "b2q_weight_register", "b2q_weight_release", "b2q_weight_shape",
     "b2q_act_bytes", "b2q_act_layout", "b2q_quantize_q8_1", "b2q_ln_quantize_q8_1",
     "b2q_mul_mat_q8_0", "b2q_mul_mat_q8_0_f32", "b2q_mul_mat_q8_0_f32_noalloc", "b2q_block_sums",
@@ -74,6 +74,7 @@ def lib():
         L.b2q_last_error.restype = C.c_char_p
         L.b2q_abi_version.restype = C.c_int
         L.b2q_launch_count.restype = C.c_uint64
+        L.b2q_graph_launch_count.restype = C.c_uint64
         L.b2q_init.argtypes = [C.c_int, C.c_int]
         L.b2q_check_device.argtypes = [P, C.POINTER(C.c_uint32)]
         L.b2q_tune.argtypes = [C.c_int, I64]
@@ -120,7 +121,7 @@ def lib():
         for name in EXPORTS:
             fn = getattr(L, name)
             if name not in ("b2q_last_error", "b2q_abi_version", "b2q_act_bytes", "b2q_attention_scratch_bytes",
-                            "b2q_launch_count"):
+                            "b2q_launch_count", "b2q_graph_launch_count"):
                 fn.restype = C.c_int
         _lib = L
     return _lib
@@ -128,6 +129,11 @@ def lib():
 
 def launch_count() -> int:
     return int(lib().b2q_launch_count())
+
+
+def graph_launch_count() -> int:
+    """Tower encodes the library launched as one captured CUDA graph."""
+    return int(lib().b2q_graph_launch_count())
 
 
 def check(status: int):
@@ -152,6 +158,7 @@ def init(device: int = 0, ops_mode: int = -1):
 
 
 TUNE_GEMM_BN, TUNE_TIMEOUT_NS, TUNE_ATTN_EXACT, TUNE_TEST_STALL, TUNE_ATTN_KERNEL, TUNE_GEMM_CTAS = 1, 2, 3, 4, 5, 6
+TUNE_GRAPHS = 7
 
 
 def tune(key: int, value: int):

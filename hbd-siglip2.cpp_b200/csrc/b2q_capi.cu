@@ -22,6 +22,10 @@ std::atomic<uint64_t> g_launches{0};
 }  // namespace
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void add_launches(int64_t n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+std::atomic<uint64_t> g_graph_launches{0};
+void count_graph_launch() { g_graph_launches.fetch_add(1, std::memory_order_relaxed); }
+uint64_t launches_now() { return g_launches.load(std::memory_order_relaxed); }
 
 b2q_status set_error(b2q_status st, const std::string& msg) {
     t_last_error = msg;
@@ -67,6 +71,7 @@ const char* b2q_last_error(void) { return t_last_error.c_str(); }
 int b2q_abi_version(void) { return 1; }
 
 uint64_t b2q_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+uint64_t b2q_graph_launch_count(void) { return g_graph_launches.load(std::memory_order_relaxed); }
 
 b2q_status b2q_init(int device, int ops_mode) {
     if (device < 0 || device >= 64) return set_error(B2Q_ERR_INVALID, "device index out of range");
@@ -105,6 +110,7 @@ b2q_status b2q_init(int device, int ops_mode) {
 
 b2q_status b2q_tune(int key, int64_t value) {
     B2Q_REQUIRE_STATE();
+    ++ds->tune_gen;   // graphs captured under the old settings are not replayed
     switch (key) {
         case B2Q_TUNE_GEMM_BN:
             if (value != 0 && value != 64 && value != 128 && value != 256)
@@ -128,6 +134,9 @@ b2q_status b2q_tune(int key, int64_t value) {
         case B2Q_TUNE_GEMM_CTAS:
             if (value != 0 && value != 1 && value != 2) return set_error(B2Q_ERR_INVALID, "GEMM CTAs per SM must be 0, 1 or 2");
             ds->gemm_ctas = static_cast<int>(value);
+            return B2Q_OK;
+        case B2Q_TUNE_GRAPHS:
+            ds->graphs = value ? 1 : 0;
             return B2Q_OK;
         default:
             return set_error(B2Q_ERR_INVALID, "unknown tuning key");

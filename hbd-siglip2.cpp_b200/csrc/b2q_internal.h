@@ -40,9 +40,14 @@ struct DeviceState {
     int attn_exact = 0;           // attention in the checker's fixed fp32 order
     int attn_kernel = 0;          // 0 = tcgen05 kernel, 1 = mma.sync kernel
     int test_stall = 0;           // GEMM producer / attention MMA issuer idle (failure-path tests)
+    int graphs = 1;               // towers replay a repeated encode as a CUDA graph
+    uint64_t tune_gen = 0;        // bumped by every b2q_tune call (captured graphs hold the settings)
 };
 DeviceState* state();             // per-thread current device state
 void count_launch();              // every kernel launch of the library counts once
+void add_launches(int64_t n);     // kernels of a replayed graph (negative: captured, not run)
+uint64_t launches_now();
+void count_graph_launch();        // a captured tower encode launched as one graph
 b2q_status set_error(b2q_status st, const std::string& msg);
 b2q_status cuda_check(cudaError_t e, const char* what);
 

@@ -133,6 +133,8 @@ struct b2q_text {
     DevBuf x, qkv16, attn, act_h, act_f, tiles, pooled, ids_in, out_dev;
     std::vector<uint8_t> host_tiles;
     int n_tiles_for = -1, n_tiles = 0;   // tile table cached for this many prompts
+    uint64_t gen = 0;                    // bumped whenever a tensor or a buffer may have moved
+    EncodeGraph graph;
 };
 
 namespace {
@@ -176,6 +178,7 @@ b2q_status b2q_text_set_tensor(b2q_text* t, const char* name, int32_t ggml_type,
     const bool table = n == "t.token_embd.weight";
     if (table && (ggml_type != 8 || ne0 != t->cfg.hidden || ne1 != t->cfg.vocab))
         return set_error(B2Q_ERR_SHAPE, "t.token_embd.weight must be Q8_0 [vocab][hidden]");
+    ++t->gen;
     return t->ts.put(n, ggml_type, host_data, ne0, ne1, table, static_cast<cudaStream_t>(stream));
 }
 
@@ -185,6 +188,7 @@ b2q_status b2q_text_reserve(b2q_text* t, int32_t max_prompts) {
     if (!t || max_prompts <= 0) return set_error(B2Q_ERR_INVALID, "bad reserve arguments");
     const int64_t P = t->cfg.n_pos, H = t->cfg.hidden, T = static_cast<int64_t>(max_prompts) * P;
     const int tiles = max_prompts * static_cast<int>((P + 63) / 64);
+    ++t->gen;
     B2Q_TRY(cuda_check(t->x.ensure(T * H * 4), "cudaMalloc(x)"));
     B2Q_TRY(cuda_check(t->qkv16.ensure(T * 3 * H * 2), "cudaMalloc(qkv)"));
     B2Q_TRY(cuda_check(t->attn.ensure(T * H * 4), "cudaMalloc(attn)"));
@@ -225,32 +229,39 @@ b2q_status b2q_text_encode(b2q_text* t, const int32_t* ids, int32_t n_prompts, f
         t->n_tiles_for = n_prompts;
     }
 
-    float* x = t->x.as<float>();
-    embed_tokens_kernel<<<static_cast<unsigned>(T), 64, 0, s>>>(t->ts.raw("t.token_embd.weight"), c.vocab,
-                                                                 static_cast<int>(H), ids,
-                                                                 t->ts.f("t.position_embd.weight"),
-                                                                 static_cast<int>(P), x, ds->err);
-    count_launch();
-    B2Q_TRY(cuda_check(cudaGetLastError(), "token embedding launch"));
+    // kernel launches only from here on: a repeated call replays them as one
+    // CUDA graph (run_graphed)
+    const std::vector<int64_t> key = {static_cast<int64_t>(ds->tune_gen), static_cast<int64_t>(t->gen), n_prompts,
+                                      reinterpret_cast<int64_t>(ids), reinterpret_cast<int64_t>(out)};
+    auto issue = [&](cudaStream_t s) -> b2q_status {
+        float* x = t->x.as<float>();
+        embed_tokens_kernel<<<static_cast<unsigned>(T), 64, 0, s>>>(t->ts.raw("t.token_embd.weight"), c.vocab,
+                                                                     static_cast<int>(H), ids,
+                                                                     t->ts.f("t.position_embd.weight"),
+                                                                     static_cast<int>(P), x, ds->err);
+        count_launch();
+        B2Q_TRY(cuda_check(cudaGetLastError(), "token embedding launch"));
 
-    // attention in the fixed fp32 order: a text embedding is one token's row,
-    // so unlike the vision heads nothing averages out the q8_1 rounding
-    // decisions a non-reproducible attention would move; at n_pos = 64 the
-    // exact kernel costs little.  Text embeddings are thereby bit-identical
-    // to the CPU checker.
-    B2Q_TRY(run_encoder_blocks(t->ts, "t.", c.n_layer, c.n_head, c.eps, T, H, x, t->qkv16.as<__half>(),
-                               t->attn.as<float>(), t->act_h.p, t->act_f.p, t->tiles.p, t->n_tiles, true, s));
+        // attention in the fixed fp32 order: a text embedding is one token's row,
+        // so unlike the vision heads nothing averages out the q8_1 rounding
+        // decisions a non-reproducible attention would move; at n_pos = 64 the
+        // exact kernel costs little.  Text embeddings are thereby bit-identical
+        // to the CPU checker.
+        B2Q_TRY(run_encoder_blocks(t->ts, "t.", c.n_layer, c.n_head, c.eps, T, H, x, t->qkv16.as<__half>(),
+                                   t->attn.as<float>(), t->act_h.p, t->act_f.p, t->tiles.p, t->n_tiles, true, s));
 
-    // final LN is per row: apply it to the pooled (last) rows only
-    float* pooled = t->pooled.as<float>();
-    last_token_kernel<<<static_cast<unsigned>(n_prompts), 96, 0, s>>>(x, static_cast<int>(H), static_cast<int>(P),
-                                                                      pooled);
-    count_launch();
-    B2Q_TRY(cuda_check(cudaGetLastError(), "pool launch"));
-    B2Q_TRY(b2q_ln_quantize_q8_1(pooled, t->ts.f("t.final_ln.weight"), t->ts.f("t.final_ln.bias"), c.eps, n_prompts,
-                                 H, t->act_h.p, nullptr, s));
-    return gemm(t->ts.w("t.head.weight"), t->act_h.p, n_prompts, out, B2Q_EPI_BIAS, t->ts.f("t.head.bias"), nullptr,
-                nullptr, 0, s);
+        // final LN is per row: apply it to the pooled (last) rows only
+        float* pooled = t->pooled.as<float>();
+        last_token_kernel<<<static_cast<unsigned>(n_prompts), 96, 0, s>>>(x, static_cast<int>(H), static_cast<int>(P),
+                                                                          pooled);
+        count_launch();
+        B2Q_TRY(cuda_check(cudaGetLastError(), "pool launch"));
+        B2Q_TRY(b2q_ln_quantize_q8_1(pooled, t->ts.f("t.final_ln.weight"), t->ts.f("t.final_ln.bias"), c.eps, n_prompts,
+                                     H, t->act_h.p, nullptr, s));
+        return gemm(t->ts.w("t.head.weight"), t->act_h.p, n_prompts, out, B2Q_EPI_BIAS, t->ts.f("t.head.bias"), nullptr,
+                    nullptr, 0, s);
+    };
+    return run_graphed(t->graph, key, s, issue);
 }
 
 b2q_status b2q_text_encode_host(b2q_text* t, const int32_t* ids_host, int32_t n_prompts, float* out_host,

@@ -218,6 +218,9 @@ struct b2q_vision {
     // skips the upload and its stream synchronisation)
     std::vector<int32_t> tables_for;
     int n_tiles = 0, n_htiles = 0;
+    // bumped whenever a tensor or a workspace buffer may have moved
+    uint64_t gen = 0;
+    EncodeGraph graph;
     const float* f(const std::string& n) const { return ts.f(n); }
     const b2q_weight* w(const std::string& n) const { return ts.w(n); }
 };
@@ -275,6 +278,7 @@ b2q_status b2q_vision_set_tensor(b2q_vision* v, const char* name, int32_t ggml_t
     (void) ds;
     if (!v || !name || !host_data) return set_error(B2Q_ERR_INVALID, "null pointer");
     const std::string n(name);
+    ++v->gen;
     B2Q_TRY(v->ts.put(n, ggml_type, host_data, ne0, ne1, false, static_cast<cudaStream_t>(stream)));
     if (n.rfind("v.head.", 0) == 0) v->probe_ready = false;
     return B2Q_OK;
@@ -286,6 +290,7 @@ b2q_status b2q_vision_reserve(b2q_vision* v, int64_t max_tokens, int32_t max_ima
     if (!v || max_tokens <= 0 || max_images <= 0) return set_error(B2Q_ERR_INVALID, "bad reserve arguments");
     const int64_t T = max_tokens, H = v->cfg.hidden;
     const int64_t tiles = T / 64 + max_images;
+    ++v->gen;
     B2Q_TRY(cuda_check(v->x.ensure(T * H * 4), "cudaMalloc(x)"));
     B2Q_TRY(cuda_check(v->pos.ensure(T * H * 4), "cudaMalloc(pos)"));
     B2Q_TRY(cuda_check(v->qkv16.ensure(T * 3 * H * 2), "cudaMalloc(qkv)"));
@@ -375,61 +380,69 @@ b2q_status b2q_vision_encode(b2q_vision* v, const float* patches, const int32_t*
         v->probe_ready = true;
     }
 
-    float* x = v->x.as<float>();
-    float* pos = v->pos.as<float>();
-    __half* qkv = v->qkv16.as<__half>();
-    float* att = v->attn.as<float>();
+    // everything from here on is kernel launches only, so a repeated call
+    // replays it as one CUDA graph (run_graphed)
+    std::vector<int64_t> key = {static_cast<int64_t>(ds->tune_gen), static_cast<int64_t>(v->gen), n_images, pooling,
+                                reinterpret_cast<int64_t>(patches), reinterpret_cast<int64_t>(out)};
+    key.insert(key.end(), grid_hw, grid_hw + 2 * n_images);
+    auto issue = [&](cudaStream_t s) -> b2q_status {
+        float* x = v->x.as<float>();
+        float* pos = v->pos.as<float>();
+        __half* qkv = v->qkv16.as<__half>();
+        float* att = v->attn.as<float>();
 
-    // ---- stem: x = (patches . W + b) + pos  (src/siglip2_vision.cpp:676-691) ----
-    {
-        int max_tok = 1;
-        for (int i = 0; i < n_images; ++i) max_tok = std::max(max_tok, grid_hw[2 * i] * grid_hw[2 * i + 1]);
-        dim3 grid(static_cast<unsigned>((max_tok + kPosTok - 1) / kPosTok), static_cast<unsigned>(n_images));
-        pos_resize_kernel<<<grid, 128, 0, s>>>(v->f("v.position_embd.weight"), c.pos_side, static_cast<int>(H),
-                                              v->imgs.as<ImageDesc>(), pos);
-        count_launch();
-        B2Q_TRY(cuda_check(cudaGetLastError(), "pos resize launch"));
-    }
-    B2Q_TRY(b2q_quantize_q8_1(patches, T, c.patch_dim, c.patch_dim, v->act_p.p, s));
-    B2Q_TRY(gemm(v->w("v.patch_embd.weight"), v->act_p.p, T, x, B2Q_EPI_BIAS_RESIDUAL, v->f("v.patch_embd.bias"),
-                 pos, nullptr, 0, s));
+        // ---- stem: x = (patches . W + b) + pos  (src/siglip2_vision.cpp:676-691) ----
+        {
+            int max_tok = 1;
+            for (int i = 0; i < n_images; ++i) max_tok = std::max(max_tok, grid_hw[2 * i] * grid_hw[2 * i + 1]);
+            dim3 grid(static_cast<unsigned>((max_tok + kPosTok - 1) / kPosTok), static_cast<unsigned>(n_images));
+            pos_resize_kernel<<<grid, 128, 0, s>>>(v->f("v.position_embd.weight"), c.pos_side, static_cast<int>(H),
+                                                  v->imgs.as<ImageDesc>(), pos);
+            count_launch();
+            B2Q_TRY(cuda_check(cudaGetLastError(), "pos resize launch"));
+        }
+        B2Q_TRY(b2q_quantize_q8_1(patches, T, c.patch_dim, c.patch_dim, v->act_p.p, s));
+        B2Q_TRY(gemm(v->w("v.patch_embd.weight"), v->act_p.p, T, x, B2Q_EPI_BIAS_RESIDUAL, v->f("v.patch_embd.bias"),
+                     pos, nullptr, 0, s));
 
-    // ---- encoder blocks ----
-    B2Q_TRY(run_encoder_blocks(v->ts, "v.", c.n_layer, c.n_head, c.eps, T, H, x, qkv, att, v->act_h.p, v->act_f.p,
-                               v->tiles.p, n_tiles, false, s));
+        // ---- encoder blocks ----
+        B2Q_TRY(run_encoder_blocks(v->ts, "v.", c.n_layer, c.n_head, c.eps, T, H, x, qkv, att, v->act_h.p, v->act_f.p,
+                                   v->tiles.p, n_tiles, false, s));
 
-    // ---- post-LN (in place) and its q8_1 planes for the head ----
-    B2Q_TRY(b2q_ln_quantize_q8_1(x, v->f("v.post_ln.weight"), v->f("v.post_ln.bias"), c.eps, T, H, v->act_h.p, x, s));
+        // ---- post-LN (in place) and its q8_1 planes for the head ----
+        B2Q_TRY(b2q_ln_quantize_q8_1(x, v->f("v.post_ln.weight"), v->f("v.post_ln.bias"), c.eps, T, H, v->act_h.p, x, s));
 
-    if (pooling == B2Q_POOL_MEAN) {
-        dim3 grid(static_cast<unsigned>((H + 127) / 128), static_cast<unsigned>(n_images));
-        mean_pool_kernel<<<grid, 128, 0, s>>>(x, static_cast<int>(H), v->imgs.as<ImageDesc>(), out);
-        count_launch();
-        return cuda_check(cudaGetLastError(), "mean pool launch");
-    }
+        if (pooling == B2Q_POOL_MEAN) {
+            dim3 grid(static_cast<unsigned>((H + 127) / 128), static_cast<unsigned>(n_images));
+            mean_pool_kernel<<<grid, 128, 0, s>>>(x, static_cast<int>(H), v->imgs.as<ImageDesc>(), out);
+            count_launch();
+            return cuda_check(cudaGetLastError(), "mean pool launch");
+        }
 
-    // ---- attention-pool head ----
-    // K and V of every token: one [T][2H] fp16 block in the qkv buffer
-    B2Q_TRY(gemm(v->w("v.head.attn_k.weight"), v->act_h.p, T, qkv, B2Q_EPI_BIAS_F16, v->f("v.head.attn_k.bias"),
-                 nullptr, nullptr, 2 * H, s));
-    B2Q_TRY(gemm(v->w("v.head.attn_v.weight"), v->act_h.p, T, qkv + H, B2Q_EPI_BIAS_F16, v->f("v.head.attn_v.bias"),
-                 nullptr, nullptr, 2 * H, s));
-    float* a = v->ha.as<float>();
-    float* a2 = v->ha2.as<float>();
-    B2Q_TRY(cuda_check(launch_attention(v->q16.as<__half>(), 0, qkv, 2 * H, qkv + H, 2 * H, v->head_tiles.p,
-                                        n_htiles, c.n_head, a, H, s),
-                       "head attention launch"));
-    // attn = o_proj(a) + b; out = attn + (fc2(gelu(fc1(LN(attn)))) + b)
-    B2Q_TRY(b2q_quantize_q8_1(a, n_images, H, H, v->act_h.p, s));
-    B2Q_TRY(gemm(v->w("v.head.attn_o.weight"), v->act_h.p, n_images, a2, B2Q_EPI_BIAS, v->f("v.head.attn_o.bias"),
-                 nullptr, nullptr, 0, s));
-    B2Q_TRY(b2q_ln_quantize_q8_1(a2, v->f("v.head.ln.weight"), v->f("v.head.ln.bias"), c.eps, n_images, H,
-                                 v->act_h.p, nullptr, s));
-    B2Q_TRY(gemm(v->w("v.head.ffn_up.weight"), v->act_h.p, n_images, nullptr, B2Q_EPI_BIAS_GELU_Q8,
-                 v->f("v.head.ffn_up.bias"), nullptr, v->act_f.p, 0, s));
-    B2Q_TRY(gemm(v->w("v.head.ffn_down.weight"), v->act_f.p, n_images, out, B2Q_EPI_BIAS_RESIDUAL,
-                 v->f("v.head.ffn_down.bias"), a2, nullptr, 0, s));
-    return B2Q_OK;
+        // ---- attention-pool head ----
+        // K and V of every token: one [T][2H] fp16 block in the qkv buffer
+        B2Q_TRY(gemm(v->w("v.head.attn_k.weight"), v->act_h.p, T, qkv, B2Q_EPI_BIAS_F16, v->f("v.head.attn_k.bias"),
+                     nullptr, nullptr, 2 * H, s));
+        B2Q_TRY(gemm(v->w("v.head.attn_v.weight"), v->act_h.p, T, qkv + H, B2Q_EPI_BIAS_F16, v->f("v.head.attn_v.bias"),
+                     nullptr, nullptr, 2 * H, s));
+        float* a = v->ha.as<float>();
+        float* a2 = v->ha2.as<float>();
+        B2Q_TRY(cuda_check(launch_attention(v->q16.as<__half>(), 0, qkv, 2 * H, qkv + H, 2 * H, v->head_tiles.p,
+                                            n_htiles, c.n_head, a, H, s),
+                           "head attention launch"));
+        // attn = o_proj(a) + b; out = attn + (fc2(gelu(fc1(LN(attn)))) + b)
+        B2Q_TRY(b2q_quantize_q8_1(a, n_images, H, H, v->act_h.p, s));
+        B2Q_TRY(gemm(v->w("v.head.attn_o.weight"), v->act_h.p, n_images, a2, B2Q_EPI_BIAS, v->f("v.head.attn_o.bias"),
+                     nullptr, nullptr, 0, s));
+        B2Q_TRY(b2q_ln_quantize_q8_1(a2, v->f("v.head.ln.weight"), v->f("v.head.ln.bias"), c.eps, n_images, H,
+                                     v->act_h.p, nullptr, s));
+        B2Q_TRY(gemm(v->w("v.head.ffn_up.weight"), v->act_h.p, n_images, nullptr, B2Q_EPI_BIAS_GELU_Q8,
+                     v->f("v.head.ffn_up.bias"), nullptr, v->act_f.p, 0, s));
+        B2Q_TRY(gemm(v->w("v.head.ffn_down.weight"), v->act_f.p, n_images, out, B2Q_EPI_BIAS_RESIDUAL,
+                     v->f("v.head.ffn_down.bias"), a2, nullptr, 0, s));
+        return B2Q_OK;
+    };
+    return run_graphed(v->graph, key, s, issue);
 }
 
 b2q_status b2q_vision_encode_host(b2q_vision* v, const float* patches_host, const int32_t* grid_hw, int32_t n_images,

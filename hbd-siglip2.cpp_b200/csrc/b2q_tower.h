@@ -10,6 +10,7 @@
 
 #include <map>
 #include <string>
+#include <vector>
 
 namespace b2q {
 
@@ -73,6 +74,92 @@ struct TensorSet {
 
 b2q_status gemm(const b2q_weight* w, const void* act, int64_t M, void* y, int kind, const float* bias,
                 const float* residual, void* act_out, int64_t ld_out, cudaStream_t s);
+
+// A tower's encode replayed as one CUDA graph.  The key names everything the
+// launches depend on (batch geometry, buffer and weight addresses through the
+// tower's generation, the device's settings through b2q_tune's generation).
+// The first call with a new key launches the kernels one by one; the second
+// captures them on the tower's own stream (so the caller's stream may be the
+// legacy default one) and every call from then on launches the captured graph
+// on the caller's stream.  A capture that the runtime refuses falls back to
+// direct launches.
+struct EncodeGraph {
+    std::vector<int64_t> key;
+    bool seen = false;              // `key` has run once without a graph
+    cudaGraphExec_t exec = nullptr;
+    uint64_t kernels = 0;           // library kernels in the graph
+    cudaStream_t capture = nullptr;
+    EncodeGraph() = default;
+    EncodeGraph(const EncodeGraph&) = delete;
+    EncodeGraph& operator=(const EncodeGraph&) = delete;
+    ~EncodeGraph() {
+        forget();
+        if (capture) cudaStreamDestroy(capture);
+    }
+    void forget() {
+        if (exec) cudaGraphExecDestroy(exec);
+        exec = nullptr;
+        seen = false;
+        key.clear();
+    }
+};
+
+// Runs `issue(stream)` (kernel launches only: no allocation, copy or
+// synchronisation) through `g`.
+template <class Issue>
+b2q_status run_graphed(EncodeGraph& g, const std::vector<int64_t>& key, cudaStream_t s, Issue&& issue) {
+    DeviceState* ds = state();
+    if (!ds->graphs) {
+        g.forget();
+        return issue(s);
+    }
+    // a caller that is capturing its own graph on `s` records the kernels itself
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        (void) cudaGetLastError();
+        return issue(s);
+    }
+    if (g.exec && key == g.key) {
+        add_launches(static_cast<int64_t>(g.kernels));
+        count_graph_launch();
+        return cuda_check(cudaGraphLaunch(g.exec, s), "graph launch");
+    }
+    if (!g.seen || key != g.key) {
+        g.forget();
+        g.key = key;
+        g.seen = true;
+        return issue(s);
+    }
+    if (!g.capture && cudaStreamCreateWithFlags(&g.capture, cudaStreamNonBlocking) != cudaSuccess) {
+        (void) cudaGetLastError();
+        g.capture = nullptr;
+        return issue(s);
+    }
+    if (cudaStreamBeginCapture(g.capture, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        (void) cudaGetLastError();
+        return issue(s);
+    }
+    const uint64_t before = launches_now();
+    const b2q_status st = issue(g.capture);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(g.capture, &graph);
+    const uint64_t kernels = launches_now() - before;
+    cudaGraphExec_t exec = nullptr;
+    const bool ok = st == B2Q_OK && e == cudaSuccess && graph &&
+                    cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+    if (graph) cudaGraphDestroy(graph);
+    if (!ok) {
+        (void) cudaGetLastError();
+        g.forget();
+        add_launches(-static_cast<int64_t>(kernels));   // captured, never run
+        if (st != B2Q_OK) return st;
+        return issue(s);   // the capture was refused: launch directly
+    }
+    g.exec = exec;
+    g.kernels = kernels;   // counted once while captured; this launch runs them once
+    count_graph_launch();
+    return cuda_check(cudaGraphLaunch(g.exec, s), "graph launch");
+}
 
 // B2Q_OK when every per-layer tensor `<prefix>blk.<l>.<suffix>` is present.
 b2q_status check_blocks(const TensorSet& ts, const char* prefix, int n_layer);

@@ -48,8 +48,11 @@ enum {
 /* Thread-local description of the last failure on this thread. */
 const char *b2q_last_error(void);
 int b2q_abi_version(void);
-/* Kernel launches this library has issued in the process (all devices). */
+/* Kernel launches this library has issued in the process (all devices);
+ * the kernels of a replayed encode graph count once per replay. */
 uint64_t b2q_launch_count(void);
+/* Tower encodes launched as one captured CUDA graph (B2Q_TUNE_GRAPHS). */
+uint64_t b2q_graph_launch_count(void);
 
 /* Per-device set-up (current device); allocates the device error word.
  * ops_mode: B2Q_OPS_I8 or B2Q_OPS_F16 (-1 = library default). */
@@ -78,14 +81,20 @@ b2q_status b2q_init(int device, int ops_mode);
  *                        per CTA), 0 = chosen per shape and epilogue (2 when
  *                        the 128-column tiles cover every SM, except for the
  *                        GELU -> q8_1 epilogue).  Every setting gives
- *                        bit-identical results. */
+ *                        bit-identical results.
+ *   B2Q_TUNE_GRAPHS:     1 (default) = a vision or text encode that repeats
+ *                        the previous call's geometry, buffers and settings
+ *                        is replayed as a CUDA graph (captured on the
+ *                        second such call), 0 = kernels launched one by one.
+ *                        Bit-identical either way. */
 enum {
     B2Q_TUNE_GEMM_BN = 1,
     B2Q_TUNE_TIMEOUT_NS = 2,
     B2Q_TUNE_ATTN_EXACT = 3,
     B2Q_TUNE_TEST_STALL = 4,
     B2Q_TUNE_ATTN_KERNEL = 5,
-    B2Q_TUNE_GEMM_CTAS = 6
+    B2Q_TUNE_GEMM_CTAS = 6,
+    B2Q_TUNE_GRAPHS = 7
 };
 b2q_status b2q_tune(int key, int64_t value);
 /* Reads (and clears) the device error word after synchronising `stream`;
