@@ -173,13 +173,13 @@ def reference_arm(args):
     total = sum(times)
     value = args.steps / total
     sample = (f"1 image of {CPU_SIDE}x{CPU_SIDE} = {CPU_SIDE * CPU_SIDE} patches per step (the 512-image "
-              "config-4 batch averages 613 patches per image), PROBE pooling")
+              "NaFlex batch averages 613 patches per image), PROBE pooling")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
-        "config": {"workload": "config-4 NaFlex batch through the 27-layer Q8_0 SigLIP2-so400m vision tower "
+        "config": {"workload": "512-image NaFlex batch through the 27-layer Q8_0 SigLIP2-so400m vision tower "
                                "(CPU sample)", "sample": sample},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -338,7 +338,7 @@ def suite(args):
     cfg = synth.TowerConfig()
     rng = np.random.default_rng(0)
 
-    # ---- config 2: GEMM sweep (ggml_mul_mat = quantize + GEMM, and GEMM alone)
+    # ---- GEMM sweep (ggml_mul_mat = quantize + GEMM, and GEMM alone)
     for (N, K) in [(1152, 1152), (3456, 1152), (4304, 1152), (1152, 4304)]:
         Kp = (K + 31) // 32 * 32
         wq = synth.quantize_q8_0((rng.standard_normal((N, K)) * 0.02).astype(np.float32), Kp)
@@ -357,7 +357,7 @@ def suite(args):
             ms_gemm = _events_ms(lambda: b2q.mul_mat(W, act, M, y), 10)
             ms_full = _events_ms(lambda: b2q.mul_mat_f32(W, x, M, K, y, scratch), 10)
             tops = 2.0 * M * N * K / (ms_gemm * 1e-3) / 1e12
-            emit({"config": "C2 GEMM", "M": M, "N": N, "K": K, "gemm_ms": ms_gemm, "gemm_tops": tops,
+            emit({"config": "GEMM sweep", "M": M, "N": N, "K": K, "gemm_ms": ms_gemm, "gemm_tops": tops,
                   "mul_mat_ms": ms_full, "mul_mat_tops": 2.0 * M * N * K / (ms_full * 1e-3) / 1e12,
                   "frac_int8": tops / i8 if i8 else None, "int8_peak_measured": i8,
                   "cpu_gops": cpu_gops, "cpu_sample": f"M=64 rows, {cores} threads"})
@@ -365,7 +365,7 @@ def suite(args):
         W.release()
     b2q.check_device()
 
-    # ---- config 1: vision tower, batch 1, 27 x 27 patches
+    # ---- vision tower, batch 1, 27 x 27 patches
     vck = synth.vision_checkpoint(cfg, seed=0)
     vt = b2q.VisionTower(cfg)
     vt.load(vck)
@@ -376,10 +376,10 @@ def suite(args):
     t = time.perf_counter()
     O.vision_encode(vck, p1, 27, 27, pooling=1)
     cpu1 = 1.0 / (time.perf_counter() - t)
-    emit({"config": "C1 vision batch 1, 729 patches", "ms_per_image": ms1, "images_per_s": 1e3 / ms1,
+    emit({"config": "vision batch 1, 729 patches", "ms_per_image": ms1, "images_per_s": 1e3 / ms1,
           "int8_tops": 604.5e9 / (ms1 * 1e-3) / 1e12, "cpu_images_per_s": cpu1, "cpu_cores": cores})
 
-    # ---- config 3: text tower, 5 prompts x 64
+    # ---- text tower, 5 prompts x 64
     tck = synth.text_checkpoint(cfg, seed=0)
     tt = b2q.TextTower(cfg)
     tt.load(tck)
@@ -390,10 +390,10 @@ def suite(args):
     t = time.perf_counter()
     O.text_encode(tck, ids)
     cpu3 = 5.0 / (time.perf_counter() - t)
-    emit({"config": "C3 text 5 x 64", "ms_per_batch": ms3, "prompts_per_s": 5e3 / ms3,
+    emit({"config": "text 5 x 64", "ms_per_batch": ms3, "prompts_per_s": 5e3 / ms3,
           "cpu_prompts_per_s": cpu3, "cpu_cores": cores})
 
-    # ---- config 5: zero-shot, 2048 images x 729 patches vs 1000 prompts, one GPU
+    # ---- zero-shot, 2048 images x 729 patches vs 1000 prompts, one GPU
     n_img, n_txt, chunk = 2048, 1000, 512
     pchunk = torch.from_numpy(np.concatenate([synth.patches(729, cfg.patch_dim, seed=10 + i)
                                               for i in range(chunk)])).cuda()
@@ -411,7 +411,7 @@ def suite(args):
 
     ms5 = _events_ms(zero_shot, 2, warm=1)
     b2q.check_device()
-    emit({"config": "C5 zero-shot 2048 images x 1000 prompts (1 GPU)", "ms": ms5,
+    emit({"config": "zero-shot 2048 images x 1000 prompts (1 GPU)", "ms": ms5,
           "images_per_s": n_img * 1e3 / ms5, "note": "patches of the 512-image chunk reused for all 4 chunks"})
     if args.out:
         Path(args.out).write_text("".join(json.dumps(d) + "\n" for d in out))
