@@ -12,9 +12,10 @@ so no separate L2 flush is needed.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 `value` is device-timed (CUDA events, max over ranks) with patches resident in
-HBM; `e2e` is the same metric through the public host-buffer entry point
-(b2q_vision_encode_host: pinned host patches in, host embeddings out) plus the
-gather.  `roofline` is the dominant kernel, the fc1 Q8_0 GEMM, timed with CUDA
+HBM; `e2e` is the same metric through the public host-buffer entry points,
+pinned host patches in and host embeddings out every step: on one GPU the
+pipelined b2q_vision_submit_host (each step's upload overlaps the previous
+step's encode), on several b2q_vision_encode_host plus the gather.  `roofline` is the dominant kernel, the fc1 Q8_0 GEMM, timed with CUDA
 events at the batch's shape.  `cpu_baseline` times the CPU restatement of the
 same tower on this host's cores on a bounded sample (the reference's ggml CPU
 path cannot be built here: its ggml submodule is empty).
@@ -597,10 +598,21 @@ def run_naflex(args, world, rank):
     out_host = np.empty((len(my_grids), cfg.hidden), np.float32)
     gathered_host = torch.empty((args.images, cfg.hidden), dtype=torch.float32, pin_memory=True)
 
+    out_pinned = torch.empty((len(my_grids), cfg.hidden), dtype=torch.float32, pin_memory=True)
+
     def step_e2e():
-        # public host-buffer entry point: pinned patches in, embeddings out
+        # public host-buffer entry points: pinned patches in, embeddings out.
+        # One rank: the pipelined entry point (this step's upload overlaps the
+        # previous step's encode; the timed region ends after the last
+        # download).  Several ranks: the synchronous one, since the host
+        # embeddings feed the gather.
         import ctypes as C
         g = np.asarray(my_grids, np.int32).reshape(-1)
+        if world == 1:
+            b2q.check(b2q.lib().b2q_vision_submit_host(tower.handle, host.data_ptr(), g.ctypes.data_as(b2q.I32P),
+                                                       len(my_grids), b2q.POOL_PROBE, out_pinned.data_ptr(),
+                                                       C.c_void_p(stream.cuda_stream)))
+            return
         b2q.check(b2q.lib().b2q_vision_encode_host(tower.handle, host.data_ptr(), g.ctypes.data_as(b2q.I32P),
                                                    len(my_grids), b2q.POOL_PROBE, out_host.ctypes.data,
                                                    C.c_void_p(stream.cuda_stream)))

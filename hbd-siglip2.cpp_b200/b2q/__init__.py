@@ -27,7 +27,7 @@ EXPORTS = [
     "b2q_mul_mat_q8_0", "b2q_mul_mat_q8_0_f32", "b2q_mul_mat_q8_0_f32_noalloc", "b2q_block_sums",
     "b2q_attention_scratch_bytes", "b2q_attention",
     "b2q_vision_create", "b2q_vision_destroy", "b2q_vision_set_tensor", "b2q_vision_reserve",
-    "b2q_vision_encode", "b2q_vision_encode_host",
+    "b2q_vision_encode", "b2q_vision_encode_host", "b2q_vision_submit_host", "b2q_vision_wait",
     "b2q_text_create", "b2q_text_destroy", "b2q_text_set_tensor", "b2q_text_reserve", "b2q_text_encode",
     "b2q_text_encode_host", "b2q_score_scratch_bytes", "b2q_score",
     "b2q_gguf_open", "b2q_gguf_close", "b2q_gguf_n_tensors", "b2q_gguf_tensor", "b2q_gguf_scalar_f32",
@@ -100,6 +100,8 @@ def lib():
         L.b2q_vision_reserve.argtypes = [P, I64, C.c_int32]
         L.b2q_vision_encode.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
         L.b2q_vision_encode_host.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
+        L.b2q_vision_submit_host.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
+        L.b2q_vision_wait.argtypes = [P, P]
         L.b2q_text_create.argtypes = [C.POINTER(TextConfig), C.POINTER(P)]
         L.b2q_text_destroy.argtypes = [P]
         L.b2q_text_set_tensor.argtypes = [P, C.c_char_p, C.c_int32, P, I64, I64, P]
@@ -145,6 +147,11 @@ def _ptr(t) -> int | None:
     if t is None:
         return None
     return t.data_ptr()
+
+
+def _host_ptr(a):
+    """Address of a host buffer: a torch CPU tensor or a numpy array."""
+    return a.data_ptr() if hasattr(a, "data_ptr") else a.ctypes.data
 
 
 def _stream(stream=None):
@@ -333,6 +340,19 @@ class VisionTower:
         check(lib().b2q_vision_encode_host(self.handle, patches.ctypes.data, gp, n, pooling, out.ctypes.data,
                                            _stream(stream)))
         return out
+
+    def submit_host(self, patches, grids, out, pooling=POOL_PROBE, stream=None):
+        """Pipelined host entry point (b2q_vision_submit_host): patches and out
+        are pinned host tensors (or any host buffers exposing data_ptr / the
+        array interface); returns without waiting, see wait()."""
+        g, gp = _i32(np.asarray(grids, np.int32).reshape(-1))
+        # the last two submissions' buffers stay referenced until their copies have run
+        self._keep = (getattr(self, "_keep", ((), ()))[-1], (g, patches, out))
+        check(lib().b2q_vision_submit_host(self.handle, _host_ptr(patches), gp, len(grids), pooling, _host_ptr(out),
+                                           _stream(stream)))
+
+    def wait(self, stream=None):
+        check(lib().b2q_vision_wait(self.handle, _stream(stream)))
 
     def close(self):
         if self.handle:

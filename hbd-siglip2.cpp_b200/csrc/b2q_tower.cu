@@ -221,6 +221,20 @@ struct b2q_vision {
     // bumped whenever a tensor or a workspace buffer may have moved
     uint64_t gen = 0;
     EncodeGraph graph;
+    // pipelined host entry point: two input / output slots, a copy stream,
+    // and per slot the events "patches landed" and "encode done"
+    DevBuf slot_in[2], slot_out[2];
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t landed[2] = {nullptr, nullptr}, done[2] = {nullptr, nullptr};
+    bool slot_busy[2] = {false, false};
+    int next_slot = 0;
+    ~b2q_vision() {
+        for (int k = 0; k < 2; ++k) {
+            if (landed[k]) cudaEventDestroy(landed[k]);
+            if (done[k]) cudaEventDestroy(done[k]);
+        }
+        if (copy_stream) cudaStreamDestroy(copy_stream);
+    }
     const float* f(const std::string& n) const { return ts.f(n); }
     const b2q_weight* w(const std::string& n) const { return ts.w(n); }
 };
@@ -465,6 +479,56 @@ b2q_status b2q_vision_encode_host(b2q_vision* v, const float* patches_host, cons
                                        cudaMemcpyDeviceToHost, s),
                        "embedding download"));
     return cuda_check(cudaStreamSynchronize(s), "encode");
+}
+
+b2q_status b2q_vision_submit_host(b2q_vision* v, const float* patches_host, const int32_t* grid_hw, int32_t n_images,
+                                  int32_t pooling, float* out_host, void* stream) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!v || !patches_host || !grid_hw || !out_host) return set_error(B2Q_ERR_INVALID, "null pointer");
+    if (n_images <= 0) return set_error(B2Q_ERR_INVALID, "n_images must be positive");
+    int64_t T = 0;
+    for (int i = 0; i < n_images; ++i) T += static_cast<int64_t>(grid_hw[2 * i]) * grid_hw[2 * i + 1];
+    if (T <= 0) return set_error(B2Q_ERR_SHAPE, "empty batch");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!v->copy_stream) {
+        B2Q_TRY(cuda_check(cudaStreamCreateWithFlags(&v->copy_stream, cudaStreamNonBlocking), "copy stream"));
+        for (int k = 0; k < 2; ++k) {
+            B2Q_TRY(cuda_check(cudaEventCreateWithFlags(&v->landed[k], cudaEventDisableTiming), "event"));
+            B2Q_TRY(cuda_check(cudaEventCreateWithFlags(&v->done[k], cudaEventDisableTiming), "event"));
+        }
+    }
+    const int k = v->next_slot;
+    const size_t in_bytes = static_cast<size_t>(T) * v->cfg.patch_dim * 4;
+    const size_t out_bytes = static_cast<size_t>(n_images) * v->cfg.hidden * 4;
+    if (in_bytes > v->slot_in[k].n || out_bytes > v->slot_out[k].n) {
+        // growing a slot frees it: its previous encode must have finished
+        if (v->slot_busy[k]) B2Q_TRY(cuda_check(cudaEventSynchronize(v->done[k]), "slot reuse"));
+        B2Q_TRY(cuda_check(v->slot_in[k].ensure(in_bytes), "cudaMalloc(patch slot)"));
+        B2Q_TRY(cuda_check(v->slot_out[k].ensure(out_bytes), "cudaMalloc(output slot)"));
+    }
+    // the upload may start once the encode that last read this slot is done;
+    // it overlaps the encode of the other slot
+    if (v->slot_busy[k]) B2Q_TRY(cuda_check(cudaStreamWaitEvent(v->copy_stream, v->done[k], 0), "slot wait"));
+    B2Q_TRY(cuda_check(cudaMemcpyAsync(v->slot_in[k].p, patches_host, in_bytes, cudaMemcpyHostToDevice, v->copy_stream),
+                       "patch upload"));
+    B2Q_TRY(cuda_check(cudaEventRecord(v->landed[k], v->copy_stream), "event record"));
+    B2Q_TRY(cuda_check(cudaStreamWaitEvent(s, v->landed[k], 0), "upload wait"));
+    B2Q_TRY(b2q_vision_encode(v, v->slot_in[k].as<float>(), grid_hw, n_images, pooling, v->slot_out[k].as<float>(),
+                              stream));
+    B2Q_TRY(cuda_check(cudaEventRecord(v->done[k], s), "event record"));
+    B2Q_TRY(cuda_check(cudaMemcpyAsync(out_host, v->slot_out[k].p, out_bytes, cudaMemcpyDeviceToHost, s),
+                       "embedding download"));
+    v->slot_busy[k] = true;
+    v->next_slot = k ^ 1;
+    return B2Q_OK;
+}
+
+b2q_status b2q_vision_wait(b2q_vision* v, void* stream) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!v) return set_error(B2Q_ERR_INVALID, "null pointer");
+    return cuda_check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "encode wait");
 }
 
 }  // extern "C"

@@ -75,19 +75,26 @@ struct TensorSet {
 b2q_status gemm(const b2q_weight* w, const void* act, int64_t M, void* y, int kind, const float* bias,
                 const float* residual, void* act_out, int64_t ld_out, cudaStream_t s);
 
-// A tower's encode replayed as one CUDA graph.  The key names everything the
-// launches depend on (batch geometry, buffer and weight addresses through the
-// tower's generation, the device's settings through b2q_tune's generation).
-// The first call with a new key launches the kernels one by one; the second
-// captures them on the tower's own stream (so the caller's stream may be the
-// legacy default one) and every call from then on launches the captured graph
-// on the caller's stream.  A capture that the runtime refuses falls back to
-// direct launches.
+// A tower's encodes replayed as CUDA graphs.  A key names everything the
+// launches depend on (batch geometry, input and output addresses, buffer and
+// weight addresses through the tower's generation, the device's settings
+// through b2q_tune's generation).  The first call with a key launches the
+// kernels one by one; the second captures them on the tower's own stream (so
+// the caller's stream may be the legacy default one) and every later call
+// launches the captured graph on the caller's stream.  Up to kEntries keys
+// are kept (the pipelined host entry point alternates between two input
+// buffers); the least recently used one is dropped.  A capture that the
+// runtime refuses falls back to direct launches.
 struct EncodeGraph {
-    std::vector<int64_t> key;
-    bool seen = false;              // `key` has run once without a graph
-    cudaGraphExec_t exec = nullptr;
-    uint64_t kernels = 0;           // library kernels in the graph
+    static constexpr int kEntries = 4;
+    struct Entry {
+        std::vector<int64_t> key;
+        cudaGraphExec_t exec = nullptr;   // null: the key has run once without a graph
+        uint64_t kernels = 0;             // library kernels in the graph
+        uint64_t used = 0;
+    };
+    std::vector<Entry> entries;
+    uint64_t clock = 0;
     cudaStream_t capture = nullptr;
     EncodeGraph() = default;
     EncodeGraph(const EncodeGraph&) = delete;
@@ -97,10 +104,25 @@ struct EncodeGraph {
         if (capture) cudaStreamDestroy(capture);
     }
     void forget() {
-        if (exec) cudaGraphExecDestroy(exec);
-        exec = nullptr;
-        seen = false;
-        key.clear();
+        for (Entry& e : entries)
+            if (e.exec) cudaGraphExecDestroy(e.exec);
+        entries.clear();
+    }
+    Entry* find(const std::vector<int64_t>& key) {
+        for (Entry& e : entries)
+            if (e.key == key) return &e;
+        return nullptr;
+    }
+    Entry& add(const std::vector<int64_t>& key) {
+        if (static_cast<int>(entries.size()) == kEntries) {
+            size_t lru = 0;
+            for (size_t i = 1; i < entries.size(); ++i)
+                if (entries[i].used < entries[lru].used) lru = i;
+            if (entries[lru].exec) cudaGraphExecDestroy(entries[lru].exec);
+            entries.erase(entries.begin() + static_cast<long>(lru));
+        }
+        entries.push_back(Entry{key, nullptr, 0, ++clock});
+        return entries.back();
     }
 };
 
@@ -119,17 +141,18 @@ b2q_status run_graphed(EncodeGraph& g, const std::vector<int64_t>& key, cudaStre
         (void) cudaGetLastError();
         return issue(s);
     }
-    if (g.exec && key == g.key) {
-        add_launches(static_cast<int64_t>(g.kernels));
+    EncodeGraph::Entry* e = g.find(key);
+    if (e && e->exec) {
+        e->used = ++g.clock;
+        add_launches(static_cast<int64_t>(e->kernels));
         count_graph_launch();
-        return cuda_check(cudaGraphLaunch(g.exec, s), "graph launch");
+        return cuda_check(cudaGraphLaunch(e->exec, s), "graph launch");
     }
-    if (!g.seen || key != g.key) {
-        g.forget();
-        g.key = key;
-        g.seen = true;
+    if (!e) {
+        g.add(key);
         return issue(s);
     }
+    e->used = ++g.clock;
     if (!g.capture && cudaStreamCreateWithFlags(&g.capture, cudaStreamNonBlocking) != cudaSuccess) {
         (void) cudaGetLastError();
         g.capture = nullptr;
@@ -142,10 +165,10 @@ b2q_status run_graphed(EncodeGraph& g, const std::vector<int64_t>& key, cudaStre
     const uint64_t before = launches_now();
     const b2q_status st = issue(g.capture);
     cudaGraph_t graph = nullptr;
-    const cudaError_t e = cudaStreamEndCapture(g.capture, &graph);
+    const cudaError_t err = cudaStreamEndCapture(g.capture, &graph);
     const uint64_t kernels = launches_now() - before;
     cudaGraphExec_t exec = nullptr;
-    const bool ok = st == B2Q_OK && e == cudaSuccess && graph &&
+    const bool ok = st == B2Q_OK && err == cudaSuccess && graph &&
                     cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
     if (graph) cudaGraphDestroy(graph);
     if (!ok) {
@@ -155,10 +178,10 @@ b2q_status run_graphed(EncodeGraph& g, const std::vector<int64_t>& key, cudaStre
         if (st != B2Q_OK) return st;
         return issue(s);   // the capture was refused: launch directly
     }
-    g.exec = exec;
-    g.kernels = kernels;   // counted once while captured; this launch runs them once
+    e->exec = exec;
+    e->kernels = kernels;   // counted once while captured; this launch runs them once
     count_graph_launch();
-    return cuda_check(cudaGraphLaunch(g.exec, s), "graph launch");
+    return cuda_check(cudaGraphLaunch(e->exec, s), "graph launch");
 }
 
 // B2Q_OK when every per-layer tensor `<prefix>blk.<l>.<suffix>` is present.

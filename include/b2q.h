@@ -240,6 +240,17 @@ b2q_status b2q_vision_encode(b2q_vision *v, const float *patches, const int32_t 
  * and synchronises `stream`. */
 b2q_status b2q_vision_encode_host(b2q_vision *v, const float *patches_host, const int32_t *grid_hw,
                                   int32_t n_images, int32_t pooling, float *out_host, void *stream);
+/* Pipelined host entry point: queues the upload of the patches (on the
+ * tower's own copy stream, into one of two device slots), the encode and the
+ * download of the embeddings (on `stream`), and returns without waiting, so
+ * the next call's upload runs while this call's encode does.  With pinned
+ * host buffers the copies overlap the kernels; `out_host` must not be read,
+ * nor `patches_host` rewritten, until b2q_vision_wait (or a synchronisation
+ * of `stream`) returns.  Results are those of b2q_vision_encode_host. */
+b2q_status b2q_vision_submit_host(b2q_vision *v, const float *patches_host, const int32_t *grid_hw,
+                                  int32_t n_images, int32_t pooling, float *out_host, void *stream);
+/* Waits for every encode submitted on `stream`. */
+b2q_status b2q_vision_wait(b2q_vision *v, void *stream);
 
 /* ---- text tower ------------------------------------------------------------
  * Batched counterpart of siglip2::TextEncoder::encode_batch

@@ -192,3 +192,24 @@ def test_caller_capture_records_the_kernels(vision):
     torch.cuda.synchronize()
     assert b2q.check_device() == 0
     assert torch.equal(out, ref)
+
+
+def test_vision_pipelined_submit_matches_encode_host(vision):
+    """b2q_vision_submit_host: two slots in flight, uploads overlapping the
+    other slot's encode; every result equals the synchronous entry point's."""
+    cfg, _, tower = vision
+    T = sum(h * w for h, w in GRIDS)
+    inputs = [torch.from_numpy(synth.patches(T, cfg.patch_dim, seed=20 + i)).pin_memory() for i in range(3)]
+    refs = [tower.encode_host(x.numpy(), GRIDS, b2q.POOL_PROBE) for x in inputs]
+    assert b2q.check_device() == 0
+    outs = [torch.empty((len(GRIDS), cfg.hidden), dtype=torch.float32).pin_memory() for _ in range(7)]
+    order = [0, 1, 2, 0, 1, 2, 0]
+    for i, o in zip(order, outs[:4]):
+        tower.submit_host(inputs[i], GRIDS, o)
+    tower.wait()
+    for i, o in zip(order[4:], outs[4:]):
+        tower.submit_host(inputs[i], GRIDS, o)
+    tower.wait()
+    assert b2q.check_device() == 0
+    for n, (i, o) in enumerate(zip(order, outs)):
+        np.testing.assert_array_equal(o.numpy(), refs[i], err_msg=f"submission {n}")
