@@ -113,8 +113,8 @@ b2q_status b2q_tune(int key, int64_t value) {
     ++ds->tune_gen;   // graphs captured under the old settings are not replayed
     switch (key) {
         case B2Q_TUNE_GEMM_BN:
-            if (value != 0 && value != 64 && value != 128 && value != 256)
-                return set_error(B2Q_ERR_INVALID, "GEMM tile width must be 0, 64, 128 or 256");
+            if (value != 0 && value != 64 && value != 128 && value != 192 && value != 256)
+                return set_error(B2Q_ERR_INVALID, "GEMM tile width must be 0, 64, 128, 192 or 256");
             ds->gemm_bn = static_cast<int>(value);
             return B2Q_OK;
         case B2Q_TUNE_TIMEOUT_NS:

@@ -55,16 +55,19 @@ struct GemmCfg {
     // per CTA, one per quadrant, each owning all of its 32 rows' columns; the
     // SM's two CTAs interleave, so one CTA's tile-end epilogue overlaps the
     // other's K-block loop.
-    static constexpr int EPI_WARPS = kCtas == 1 ? 8 : 4;
-    static constexpr int THREADS = 128 + EPI_WARPS * 32;   // 384 or 256
-    static constexpr int LAUNCH_REGS = kCtas == 1 ? 168 : 128;
-    static constexpr int WG0_REGS = kCtas == 1 ? 40 : 24;  // producer / MMA warpgroup after setmaxnreg
-    static constexpr int EPI_REGS = 232;
+    // 192-column tiles: twelve epilogue warps, three per TMEM lane quadrant
+    // (and SMSP), each owning 64 of the tile's columns (run_epilogue_w12).
+    static constexpr bool W12 = kCtas == 1 && kBN == 192;
+    static constexpr int EPI_WARPS = W12 ? 12 : (kCtas == 1 ? 8 : 4);
+    static constexpr int THREADS = 128 + EPI_WARPS * 32;   // 512, 384 or 256
+    static constexpr int LAUNCH_REGS = kCtas == 1 && !W12 ? 168 : 128;
+    static constexpr int WG0_REGS = kCtas == 1 && !W12 ? 40 : 24;   // producer / MMA warpgroup after setmaxnreg
+    static constexpr int EPI_REGS = W12 ? 160 : 232;
     static constexpr int COLS = BN * 4 / EPI_WARPS;        // columns per epilogue thread
     static constexpr int CC = COLS / 64;                   // 64-column chunks per epilogue thread
     static constexpr int CH = 2 * CC;                      // 16x256b.x8 TMEM loads per K block (2 slabs)
     static constexpr int TMEM_COLS = 512 / kCtas;
-    static constexpr int NBUF = TMEM_COLS / BN;            // accumulator ring depth
+    static constexpr int NBUF = TMEM_COLS / BN;            // accumulator ring depth (192 columns: two, 128 unused)
     static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment for the swizzle");
     static_assert(CH % 2 == 0, "register double-buffer parity must repeat every K block");
     static_assert(NBUF >= 2, "the accumulator ring needs two buffers");
@@ -537,6 +540,80 @@ __device__ bool run_epilogue(const Smem& sm, uint32_t tmem_base, const GemmParam
     return true;
 }
 
+
+// 192-column tiles, twelve epilogue warps (three per SMSP): each thread holds
+// 4 rows x 16 columns, and a K block is one short chain per warp: wait for
+// the accumulator, both 16-lane slabs' loads and the block's scales issued
+// together, one wait, the buffer released at once (before the arithmetic),
+// then 64 packed rescale instructions.  The SMSP's other two epilogue warps
+// cover the chain's latencies, so the loop carries no intra-warp double
+// buffering and no early probes, which leaves about 85 other instructions
+// per block (against ~180 in the two-warp loop above); the stage is released
+// once every lane has used its scales.
+template <int kOps>
+__device__ bool run_epilogue_w12(const Smem& sm, uint32_t tmem_base, const GemmParams& p, int warp, int lane) {
+    using Cfg = GemmCfg<kOps, 192, 1>;
+    const int ew = warp - 4;
+    const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
+    const int col0 = (ew >> 2) * 64;            // first of this warp's 64 columns
+    const int q = lane & 3;
+    const int rloc = quad * 32 + (lane >> 2);
+    const uint32_t taddr0 = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + col0;
+    const uint32_t dx_off = Cfg::A_BYTES + Cfg::B_BYTES + rloc * 4;
+    // dW[j][slot]: this thread's 16-byte vectors sit at slots 16i + 4q of its 64-column group
+    const uint32_t dw_off = Cfg::A_BYTES + Cfg::B_BYTES + Cfg::DX_BYTES + (col0 + 4 * q) * 4;
+    const int num_tiles = p.m_tiles * p.n_tiles;
+    Ring<Cfg::NBUF> acc_ring;
+    Ring<Cfg::STAGES> st_ring;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int mb = tile / p.n_tiles, nb = tile - (tile / p.n_tiles) * p.n_tiles + p.nb_off;
+        const int mrow0 = mb * Cfg::BM + rloc;
+        const int nblk0 = nb * Cfg::BN + col0;
+        float2 acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.0f, 0.0f);
+        int j = 0;   // K block inside the current stage
+        for (int kb = 0; kb < p.Kb; ++kb) {
+            if (j == 0 && !mbar_wait(bar_at(sm.full, st_ring.idx), st_ring.phase, sm.abort_flag, p.timeout_ns)) {
+                raise_error(p.err, sm.abort_flag, kDevTimeoutFull);
+                return false;
+            }
+            if (!mbar_wait(bar_at(sm.tfull, acc_ring.idx), acc_ring.phase, sm.abort_flag, p.timeout_ns)) {
+                raise_error(p.err, sm.abort_flag, kDevTimeoutTmemFull);
+                return false;
+            }
+            tc_fence_after();
+            uint32_t r0[32], r1[32];
+            const uint32_t ta = taddr0 + acc_ring.idx * Cfg::BN;
+            tmem_ld_16x256b_x8(ta, r0);
+            tmem_ld_16x256b_x8(ta + (16u << 16), r1);
+            const uint32_t sb = sm.base + st_ring.idx * Cfg::STAGE_BYTES;
+            const uint32_t sdx = sb + dx_off + j * Cfg::BM * 4;   // rows +0, +8, +16, +24
+            const float d00 = lds_f32(sdx), d01 = lds_f32(sdx + 32), d10 = lds_f32(sdx + 64), d11 = lds_f32(sdx + 96);
+            const uint32_t sdw = sb + dw_off + j * Cfg::BN * 4;
+            float4 wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) wv[i] = lds_v4_f32(sdw + 64 * i);
+            tmem_ld_wait_regs(r0);
+            tmem_ld_wait_regs(r1);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_at(sm.tempty, acc_ring.idx));
+            acc_ring.next();
+            rescale_chunk<kOps>(acc, r0, wv, make_float2(d00, d00), make_float2(d01, d01));
+            rescale_chunk<kOps>(acc + 16, r1, wv, make_float2(d10, d10), make_float2(d11, d11));
+            if (++j == Cfg::KBS || kb + 1 == p.Kb) {   // every lane has used this stage's scales
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar_at(sm.empty, st_ring.idx));
+                st_ring.next();
+                j = 0;
+            }
+        }
+        store_tile<kOps, 192, 1>(p, acc, mrow0, nblk0, q);
+    }
+    return true;
+}
+
 template <int kOps, int kBN, int kCtas, bool kDump>
 __global__ void __launch_bounds__(GemmCfg<kOps, kBN, kCtas>::THREADS, kCtas)
 gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -607,7 +684,10 @@ gemm_q8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else {
         warpgroup_reg_alloc<Cfg::EPI_REGS>();
-        run_epilogue<kOps, kBN, kCtas, kDump>(sm, tmem_base, p, warp, lane);
+        if constexpr (Cfg::W12 && !kDump)
+            run_epilogue_w12<kOps>(sm, tmem_base, p, warp, lane);
+        else
+            run_epilogue<kOps, kBN, kCtas, kDump>(sm, tmem_base, p, warp, lane);
         // an epilogue that gave up on an expired wait may still have a TMEM
         // load in flight: let it land before TMEM is released
         tmem_ld_wait();
@@ -649,8 +729,8 @@ static b2q_status run_gemm(const GemmArgs& a, cudaStream_t s, int64_t n_base, in
         !make_tmap_2d(&tmDX, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act + L.d_offset, L.M, L.Kb, L.ld * 4, Cfg::BM,
                       Cfg::KBS, false))
         return set_error(B2Q_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation planes");
-    const CUtensorMap* tmB = kBN == 256 ? &w->tm_q256 : kBN == 128 ? &w->tm_q128 : &w->tm_q64;
-    const CUtensorMap* tmDW = kBN == 256 ? &w->tm_d256 : kBN == 128 ? &w->tm_d128 : &w->tm_d64;
+    const CUtensorMap* tmB = kBN == 256 ? &w->tm_q256 : kBN == 192 ? &w->tm_q192 : kBN == 128 ? &w->tm_q128 : &w->tm_q64;
+    const CUtensorMap* tmDW = kBN == 256 ? &w->tm_d256 : kBN == 192 ? &w->tm_d192 : kBN == 128 ? &w->tm_d128 : &w->tm_d64;
 
     GemmParams p{};
     p.M = static_cast<int>(a.M);
@@ -701,6 +781,7 @@ static b2q_status dispatch_bn(const GemmArgs& a, cudaStream_t s, int bn, int cta
     const int64_t N = a.w->N;
     if (a.dump) return run_gemm<kOps, 128, 1, true>(a, s, 0, N);
     if (bn == 64) return run_gemm<kOps, 64, 2, false>(a, s, 0, N);   // 64-column tiles exist in the two-CTA form
+    if (bn == 192) return run_gemm<kOps, 192, 1, false>(a, s, 0, N);  // 192-column tiles: one CTA, twelve epilogue warps
     if (ctas == 2) return run_gemm<kOps, 128, 2, false>(a, s, 0, N);
     if (bn != 256) return run_gemm<kOps, 128, 1, false>(a, s, 0, N);
     const int64_t rem = split ? split_remainder(N) : 0;
@@ -747,9 +828,36 @@ static bool small_tiles(int64_t M, int64_t N, int num_sms) {
     return ((M + 127) / 128) * ((N + 127) / 128) < num_sms;
 }
 
+// 192-column tiles (one CTA per SM, twelve epilogue warps) against the
+// layout chosen otherwise, by the tile rounds each needs: at large M a
+// 192-column tile takes about 0.714 of the time of a pair of co-resident
+// 128-column tiles (measured: +3 to +8% over the two-CTA and 256-column
+// layouts at 65,536 and 313,755 tokens, bit-identical), so they win unless
+// their last round is mostly empty; with fewer 128-column tiles than SMs
+// (the 64-column regime) they win when one round of them replaces two or
+// more rounds of 64-column tiles (QKV and fc1 at 729 tokens: +23%).
+static bool use_w12(int64_t M, int64_t N, int epi, int num_sms) {
+    const int64_t mt = (M + 127) / 128;
+    const int64_t t192 = mt * ((N + 191) / 192);
+    const double r192 = 0.714 * static_cast<double>((t192 + num_sms - 1) / num_sms);
+    if (small_tiles(M, N, num_sms)) {
+        const int64_t t64 = mt * ((N + 63) / 64);
+        return t192 <= num_sms && t64 > 2 * num_sms;
+    }
+    double other;
+    if (epi == B2Q_EPI_BIAS_GELU_Q8) {
+        other = static_cast<double>((mt * ((N + 255) / 256) + num_sms - 1) / num_sms);
+    } else {
+        other = static_cast<double>((mt * ((N + 127) / 128) + 2 * num_sms - 1) / (2 * num_sms));
+    }
+    return r192 < 0.98 * other;
+}
+
 b2q_status launch_gemm(const GemmArgs& a, cudaStream_t s) {
     DeviceState* ds = state();
-    const bool forced = ds->gemm_bn == 64 || ds->gemm_bn == 128 || ds->gemm_bn == 256;
+    const bool forced = ds->gemm_bn == 64 || ds->gemm_bn == 128 || ds->gemm_bn == 192 || ds->gemm_bn == 256;
+    if (!forced && ds->gemm_ctas == 0 && use_w12(a.M, a.w->N, a.epi, ds->num_sms))
+        return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, 192, 1, false) : dispatch_bn<kOpsI8>(a, s, 192, 1, false);
     if (!forced && ds->gemm_ctas == 0 && small_tiles(a.M, a.w->N, ds->num_sms))
         return a.w->mode == kOpsF16 ? dispatch_bn<kOpsF16>(a, s, 64, 2, false) : dispatch_bn<kOpsI8>(a, s, 64, 2, false);
     const int bn = forced ? ds->gemm_bn : auto_bn(a.M, a.w->N, ds->num_sms);
@@ -767,10 +875,12 @@ bool make_weight_maps(b2q_weight* w) {
     const uint32_t kbs = 128 / (32 * es);
     const CUtensorMapDataType dt = w->mode == kOpsF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
     return make_tmap_2d(&w->tm_q256, dt, w->q, w->K, w->N, w->K * es, 128 / es, 256, true) &&
+           make_tmap_2d(&w->tm_q192, dt, w->q, w->K, w->N, w->K * es, 128 / es, 192, true) &&
            make_tmap_2d(&w->tm_q128, dt, w->q, w->K, w->N, w->K * es, 128 / es, 128, true) &&
            make_tmap_2d(&w->tm_q64, dt, w->q, w->K, w->N, w->K * es, 128 / es, 64, true) &&
            make_tmap_2d(&w->tm_d64, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 64, kbs, false) &&
            make_tmap_2d(&w->tm_d256, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 256, kbs, false) &&
+           make_tmap_2d(&w->tm_d192, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 192, kbs, false) &&
            make_tmap_2d(&w->tm_d128, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->d, w->Nd, w->Kb, w->Nd * 4, 128, kbs, false);
 }
 

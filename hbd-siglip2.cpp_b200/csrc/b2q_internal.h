@@ -66,8 +66,8 @@ struct b2q_weight {
     void* q = nullptr;     // [N][K] int8 (or fp16 carriers)
     float* d = nullptr;    // [Kb][Nd] fp32 (exact widening of the fp16 scales), columns
                            // permuted inside each 64-column group (scale_slot)
-    CUtensorMap tm_q256, tm_q128, tm_q64;   // box 128 B x {256,128,64} rows, 128-byte swizzle
-    CUtensorMap tm_d256, tm_d128, tm_d64;   // box {256,128,64} x (scales per stage)
+    CUtensorMap tm_q256, tm_q192, tm_q128, tm_q64;   // box 128 B x {256,192,128,64} rows, 128-byte swizzle
+    CUtensorMap tm_d256, tm_d192, tm_d128, tm_d64;   // box {256,192,128,64} x (scales per stage)
 };
 
 // Position of column n inside its 64-column group of the weight-scale rows.

@@ -59,12 +59,13 @@ uint64_t b2q_graph_launch_count(void);
 b2q_status b2q_init(int device, int ops_mode);
 /* Tuning knobs of the current device's state (reference precedent: the
  * SIGLIP2_* environment switches of src/cuda/siglip2_megakernel.cu:1378-1401).
- *   B2Q_TUNE_GEMM_BN:    GEMM tile width 64 (two CTAs per SM), 128 or 256
- *                        (0 = chosen per shape: 64-column tiles when
+ *   B2Q_TUNE_GEMM_BN:    GEMM tile width 64 (two CTAs per SM), 128, 192
+ *                        (one CTA per SM, twelve epilogue warps) or 256
+ *                        (0 = chosen per shape by the tile rounds each
+ *                        layout needs: 192 at large M and for the wide
+ *                        projections at small M, 64-column tiles when
  *                        128-column ones would not cover every SM, else 128
- *                        with two CTAs per SM except for the GELU epilogue,
- *                        else 256 unless 128-column tiles fill the SMs' tile
- *                        rounds sooner)
+ *                        with two CTAs per SM, or 256 for the GELU epilogue)
  *   B2Q_TUNE_TIMEOUT_NS: bound of every in-kernel wait (default 2 s)
  *   B2Q_TUNE_ATTN_EXACT: 1 = attention in one fixed fp32 order (slow; makes
  *                        the tower bit-reproducible), 0 = tensor cores

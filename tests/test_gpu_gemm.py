@@ -18,9 +18,10 @@ torch = pytest.importorskip("torch")
 
 @pytest.fixture(scope="module", params=[(b2q.OPS_F16, 0, 0), (b2q.OPS_I8, 0, 0), (b2q.OPS_F16, 128, 1),
                                         (b2q.OPS_I8, 256, 1), (b2q.OPS_F16, 0, 1), (b2q.OPS_F16, 0, 2),
-                                        (b2q.OPS_I8, 0, 2), (b2q.OPS_F16, 64, 2), (b2q.OPS_I8, 64, 2)],
+                                        (b2q.OPS_I8, 0, 2), (b2q.OPS_F16, 64, 2), (b2q.OPS_I8, 64, 2),
+                                        (b2q.OPS_F16, 192, 1), (b2q.OPS_I8, 192, 1)],
                 ids=["f16-auto", "i8-auto", "f16-bn128", "i8-bn256", "f16-1cta", "f16-2cta", "i8-2cta", "f16-bn64",
-                     "i8-bn64"])
+                     "i8-bn64", "f16-bn192", "i8-bn192"])
 def mode(request):
     """(operand carriers, tile width, CTAs per SM); 0 = the library's choice."""
     if not torch.cuda.is_available():
