@@ -41,10 +41,10 @@ N_IMAGES = 512
 CPU_SIDE = 25        # CPU samples: one 25x25-patch image, nearest square to the batch's mean patch count
 PATCH_DIM = 768
 # DRAM bytes per token of one fc1 launch: dram__bytes_read + dram__bytes_write
-# = 171.15 + 548.74 MB from one ncu capture (one pass) of
-# `bench.py --profile-gemm 65536`, scaled to the batch's token count (the
-# traffic grows in proportion to M).
-FC1_DRAM_BYTES_PER_TOKEN = (171.15e6 + 548.74e6) / 65536
+# = 171.99 + 551.98 MB from one ncu capture (one pass) of
+# `bench.py --profile-gemm 65536` (192-column tiles), scaled to the batch's
+# token count (the traffic grows in proportion to M).
+FC1_DRAM_BYTES_PER_TOKEN = (171.99e6 + 551.98e6) / 65536
 
 
 def log(*a):
