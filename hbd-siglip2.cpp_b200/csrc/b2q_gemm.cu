@@ -61,7 +61,7 @@ struct GemmCfg {
     static constexpr int EPI_WARPS = W12 ? 12 : (kCtas == 1 ? 8 : 4);
     static constexpr int THREADS = 128 + EPI_WARPS * 32;   // 512, 384 or 256
     static constexpr int LAUNCH_REGS = kCtas == 1 && !W12 ? 168 : 128;
-    static constexpr int WG0_REGS = kCtas == 1 && !W12 ? 40 : 24;   // producer / MMA warpgroup after setmaxnreg
+    static constexpr int WG0_REGS = W12 ? 32 : (kCtas == 1 ? 40 : 24);   // producer / MMA warpgroup after setmaxnreg
     static constexpr int EPI_REGS = W12 ? 160 : 232;
     static constexpr int COLS = BN * 4 / EPI_WARPS;        // columns per epilogue thread
     static constexpr int CC = COLS / 64;                   // 64-column chunks per epilogue thread
