@@ -15,7 +15,8 @@ so no separate L2 flush is needed.
 HBM; `e2e` is the same metric through the public host-buffer entry points,
 pinned host patches in and host embeddings out every step: on one GPU the
 pipelined b2q_vision_submit_host (each step's upload overlaps the previous
-step's encode), on several b2q_vision_encode_host plus the gather.  `roofline` is the dominant kernel, the fc1 Q8_0 GEMM, timed with CUDA
+step's encode), on several the same with b2q_vision_wait_submitted, each
+step's embeddings gathered on a side stream while the next step encodes.  `roofline` is the dominant kernel, the fc1 Q8_0 GEMM, timed with CUDA
 events at the batch's shape.  `cpu_baseline` times the CPU restatement of the
 same tower on this host's cores on a bounded sample (the reference's ggml CPU
 path cannot be built here: its ggml submodule is empty).
@@ -595,32 +596,65 @@ def run_naflex(args, world, rank):
         tower.encode(dev, my_grids, b2q.POOL_PROBE, out=emb)
         gather(record)
 
-    out_host = np.empty((len(my_grids), cfg.hidden), np.float32)
     gathered_host = torch.empty((args.images, cfg.hidden), dtype=torch.float32, pin_memory=True)
 
     out_pinned = torch.empty((len(my_grids), cfg.hidden), dtype=torch.float32, pin_memory=True)
 
     def step_e2e():
-        # public host-buffer entry points: pinned patches in, embeddings out.
-        # One rank: the pipelined entry point (this step's upload overlaps the
-        # previous step's encode; the timed region ends after the last
-        # download).  Several ranks: the synchronous one, since the host
-        # embeddings feed the gather.
+        # public host-buffer entry point, one rank: pinned patches in,
+        # embeddings out, pipelined (this step's upload overlaps the previous
+        # step's encode; the timed region ends after the last download).
+        # Several ranks: e2e_pipelined below.
         import ctypes as C
         g = np.asarray(my_grids, np.int32).reshape(-1)
-        if world == 1:
-            b2q.check(b2q.lib().b2q_vision_submit_host(tower.handle, host.data_ptr(), g.ctypes.data_as(b2q.I32P),
-                                                       len(my_grids), b2q.POOL_PROBE, out_pinned.data_ptr(),
-                                                       C.c_void_p(stream.cuda_stream)))
-            return
-        b2q.check(b2q.lib().b2q_vision_encode_host(tower.handle, host.data_ptr(), g.ctypes.data_as(b2q.I32P),
-                                                   len(my_grids), b2q.POOL_PROBE, out_host.ctypes.data,
+        b2q.check(b2q.lib().b2q_vision_submit_host(tower.handle, host.data_ptr(), g.ctypes.data_as(b2q.I32P),
+                                                   len(my_grids), b2q.POOL_PROBE, out_pinned.data_ptr(),
                                                    C.c_void_p(stream.cuda_stream)))
-        if world > 1:
-            emb[:len(my_grids)].copy_(torch.from_numpy(out_host), non_blocking=False)
+
+    # Several ranks: each step's embeddings feed the gather, so the step is
+    # pipelined across the host-buffer entry points: submit batch i (its
+    # upload runs under batch i - 1's encode), wait for batch i - 1's
+    # download, gather it on a side stream while batch i encodes.  Every
+    # step's upload, download and gather falls inside the timed region
+    # (events on `stream`, which waits for the side stream at the end).
+    out_pin = [torch.empty((len(my_grids), cfg.hidden), dtype=torch.float32, pin_memory=True) for _ in range(2)]
+    side = torch.cuda.Stream() if world > 1 else None
+
+    def submit(i):
+        import ctypes as C
+        g = np.asarray(my_grids, np.int32).reshape(-1)
+        b2q.check(b2q.lib().b2q_vision_submit_host(tower.handle, host.data_ptr(), g.ctypes.data_as(b2q.I32P),
+                                                   len(my_grids), b2q.POOL_PROBE, out_pin[i % 2].data_ptr(),
+                                                   C.c_void_p(stream.cuda_stream)))
+
+    def consume(i):
+        with torch.cuda.stream(side):
+            # a blocking copy: the pinned buffer is free again when it returns
+            emb[:len(my_grids)].copy_(out_pin[i % 2], non_blocking=False)
             allemb = gather_in_order(emb[:len(mine)], mine_dev, args.images)
             if rank == 0:
-                gathered_host.copy_(allemb)
+                gathered_host.copy_(allemb, non_blocking=True)
+
+    def e2e_pipelined(steps):
+        import torch.distributed as dist
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            submit(i)
+            if i > 0:
+                tower.wait_submitted(1)
+                consume(i - 1)
+        tower.wait_submitted(0)
+        consume(steps - 1)
+        stream.wait_stream(side)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        t = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     for _ in range(args.warmup):
         step_device()
@@ -636,9 +670,13 @@ def run_naflex(args, world, rank):
     b2q.check_device()
     gather_ms = (sum(a.elapsed_time(b) for a, b in gather_events) / len(gather_events)) if gather_events else 0.0
 
-    # end to end through the host-buffer entry point
-    step_e2e()
-    ms_e2e, _ = timed(step_e2e, args.steps, stream, world)
+    # end to end through the host-buffer entry points
+    if world == 1:
+        step_e2e()
+        ms_e2e, _ = timed(step_e2e, args.steps, stream, world)
+    else:
+        e2e_pipelined(2)
+        ms_e2e = e2e_pipelined(args.steps)
 
     # roofline of the dominant kernel: fc1 GEMM (N=4304, K=1152) with the
     # GELU->q8_1 epilogue at this rank's token count, CUDA events on the stream

@@ -28,6 +28,7 @@ EXPORTS = [
     "b2q_attention_scratch_bytes", "b2q_attention",
     "b2q_vision_create", "b2q_vision_destroy", "b2q_vision_set_tensor", "b2q_vision_reserve",
     "b2q_vision_encode", "b2q_vision_encode_host", "b2q_vision_submit_host", "b2q_vision_wait",
+    "b2q_vision_wait_submitted",
     "b2q_text_create", "b2q_text_destroy", "b2q_text_set_tensor", "b2q_text_reserve", "b2q_text_encode",
     "b2q_text_encode_host", "b2q_score_scratch_bytes", "b2q_score",
     "b2q_gguf_open", "b2q_gguf_close", "b2q_gguf_n_tensors", "b2q_gguf_tensor", "b2q_gguf_scalar_f32",
@@ -102,6 +103,7 @@ def lib():
         L.b2q_vision_encode_host.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
         L.b2q_vision_submit_host.argtypes = [P, P, I32P, C.c_int32, C.c_int32, P, P]
         L.b2q_vision_wait.argtypes = [P, P]
+        L.b2q_vision_wait_submitted.argtypes = [P, C.c_int32]
         L.b2q_text_create.argtypes = [C.POINTER(TextConfig), C.POINTER(P)]
         L.b2q_text_destroy.argtypes = [P]
         L.b2q_text_set_tensor.argtypes = [P, C.c_char_p, C.c_int32, P, I64, I64, P]
@@ -353,6 +355,10 @@ class VisionTower:
 
     def wait(self, stream=None):
         check(lib().b2q_vision_wait(self.handle, _stream(stream)))
+
+    def wait_submitted(self, back=0):
+        """Wait for one submission's embeddings: back 0 = the latest, 1 = the one before."""
+        check(lib().b2q_vision_wait_submitted(self.handle, back))
 
     def close(self):
         if self.handle:

@@ -225,13 +225,14 @@ struct b2q_vision {
     // and per slot the events "patches landed" and "encode done"
     DevBuf slot_in[2], slot_out[2];
     cudaStream_t copy_stream = nullptr;
-    cudaEvent_t landed[2] = {nullptr, nullptr}, done[2] = {nullptr, nullptr};
+    cudaEvent_t landed[2] = {nullptr, nullptr}, done[2] = {nullptr, nullptr}, fetched[2] = {nullptr, nullptr};
     bool slot_busy[2] = {false, false};
     int next_slot = 0;
     ~b2q_vision() {
         for (int k = 0; k < 2; ++k) {
             if (landed[k]) cudaEventDestroy(landed[k]);
             if (done[k]) cudaEventDestroy(done[k]);
+            if (fetched[k]) cudaEventDestroy(fetched[k]);
         }
         if (copy_stream) cudaStreamDestroy(copy_stream);
     }
@@ -496,6 +497,7 @@ b2q_status b2q_vision_submit_host(b2q_vision* v, const float* patches_host, cons
         for (int k = 0; k < 2; ++k) {
             B2Q_TRY(cuda_check(cudaEventCreateWithFlags(&v->landed[k], cudaEventDisableTiming), "event"));
             B2Q_TRY(cuda_check(cudaEventCreateWithFlags(&v->done[k], cudaEventDisableTiming), "event"));
+            B2Q_TRY(cuda_check(cudaEventCreateWithFlags(&v->fetched[k], cudaEventDisableTiming), "event"));
         }
     }
     const int k = v->next_slot;
@@ -519,9 +521,20 @@ b2q_status b2q_vision_submit_host(b2q_vision* v, const float* patches_host, cons
     B2Q_TRY(cuda_check(cudaEventRecord(v->done[k], s), "event record"));
     B2Q_TRY(cuda_check(cudaMemcpyAsync(out_host, v->slot_out[k].p, out_bytes, cudaMemcpyDeviceToHost, s),
                        "embedding download"));
+    B2Q_TRY(cuda_check(cudaEventRecord(v->fetched[k], s), "event record"));
     v->slot_busy[k] = true;
     v->next_slot = k ^ 1;
     return B2Q_OK;
+}
+
+b2q_status b2q_vision_wait_submitted(b2q_vision* v, int32_t back) {
+    B2Q_REQUIRE_STATE();
+    (void) ds;
+    if (!v) return set_error(B2Q_ERR_INVALID, "null pointer");
+    if (back != 0 && back != 1) return set_error(B2Q_ERR_INVALID, "back must be 0 (latest) or 1 (the one before)");
+    const int k = back == 0 ? (v->next_slot ^ 1) : v->next_slot;   // next_slot is the older of the two
+    if (!v->slot_busy[k]) return set_error(B2Q_ERR_INVALID, "no such submission");
+    return cuda_check(cudaEventSynchronize(v->fetched[k]), "submission wait");
 }
 
 b2q_status b2q_vision_wait(b2q_vision* v, void* stream) {

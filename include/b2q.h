@@ -252,6 +252,12 @@ b2q_status b2q_vision_submit_host(b2q_vision *v, const float *patches_host, cons
                                   int32_t n_images, int32_t pooling, float *out_host, void *stream);
 /* Waits for every encode submitted on `stream`. */
 b2q_status b2q_vision_wait(b2q_vision *v, void *stream);
+/* Waits for one submission's embeddings to be in its host buffer: back = 0
+ * the latest b2q_vision_submit_host call, 1 the one before it.  A caller that
+ * consumes each batch's embeddings (a gather across GPUs, a reply) submits
+ * batch i + 1, waits with back = 1 and handles batch i while batch i + 1's
+ * encode runs. */
+b2q_status b2q_vision_wait_submitted(b2q_vision *v, int32_t back);
 
 /* ---- text tower ------------------------------------------------------------
  * Batched counterpart of siglip2::TextEncoder::encode_batch

@@ -213,3 +213,23 @@ def test_vision_pipelined_submit_matches_encode_host(vision):
     assert b2q.check_device() == 0
     for n, (i, o) in enumerate(zip(order, outs)):
         np.testing.assert_array_equal(o.numpy(), refs[i], err_msg=f"submission {n}")
+
+
+def test_vision_wait_submitted_orders_the_results(vision):
+    """b2q_vision_wait_submitted(back=1) hands over the batch before the latest
+    submission while the latest one still runs; each batch's embeddings equal
+    the synchronous entry point's."""
+    cfg, _, tower = vision
+    T = sum(h * w for h, w in GRIDS)
+    inputs = [torch.from_numpy(synth.patches(T, cfg.patch_dim, seed=30 + i)).pin_memory() for i in range(2)]
+    refs = [tower.encode_host(x.numpy(), GRIDS, b2q.POOL_PROBE) for x in inputs]
+    outs = [torch.empty((len(GRIDS), cfg.hidden), dtype=torch.float32).pin_memory() for _ in range(2)]
+    order = [0, 1, 1, 0, 0, 1]
+    for i, src in enumerate(order):
+        tower.submit_host(inputs[src], GRIDS, outs[i % 2])
+        if i > 0:
+            tower.wait_submitted(1)
+            np.testing.assert_array_equal(outs[(i - 1) % 2].numpy(), refs[order[i - 1]], err_msg=f"batch {i - 1}")
+    tower.wait_submitted(0)
+    np.testing.assert_array_equal(outs[(len(order) - 1) % 2].numpy(), refs[order[-1]])
+    assert b2q.check_device() == 0
